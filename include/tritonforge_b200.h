@@ -1,0 +1,143 @@
+/*
+ * tritonforge_b200 -- C ABI of the B200 (sm_100a) int4 decode/prefill kernels.
+ *
+ * Every entry point takes caller-owned device pointers, plain sizes and a CUDA
+ * stream (passed as `void*`, a `cudaStream_t`), launches asynchronously on that
+ * stream, never allocates and never synchronises. Each returns a tf_status
+ * code; the text of the last failure on the calling thread is available from
+ * tf_last_error_message().
+ *
+ * Weight format (identical to the reference's `src/tritonforge/quant.py`):
+ *   packed  uint8 [K_pad/2, N]   packed[j, n] = code(2j, n) | code(2j+1, n) << 4
+ *   scales  half  [K_pad/g, N]   fp16 or bf16 (`param_dtype`)
+ *   zeros   half  [K_pad/g, N]   integral values 0..15, same dtype as scales
+ *   W[k, n] = (code(k, n) - zeros[k/g, n]) * scales[k/g, n]
+ * All 2-D arrays are row-major and contiguous unless a leading dimension is
+ * passed.
+ */
+#ifndef TRITONFORGE_B200_H
+#define TRITONFORGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes and element types ---------------------------------- */
+typedef enum tf_status {
+  TF_OK = 0,
+  TF_ERR_BAD_SHAPE = 1,   /* shapes inconsistent (reference raises ValueError) */
+  TF_ERR_BAD_DTYPE = 2,   /* unsupported element type (reference: ValueError)  */
+  TF_ERR_UNALIGNED = 3,   /* pointer/stride alignment the kernel needs is missing */
+  TF_ERR_CUDA = 4,        /* a CUDA runtime call or launch failed              */
+  TF_ERR_TIMEOUT = 5,     /* a bounded device-side wait expired                 */
+  TF_ERR_WORKSPACE = 6,   /* workspace missing or smaller than required         */
+  TF_ERR_BAD_ARG = 7,     /* other invalid argument (null pointer, bad group)   */
+  TF_ERR_UNSUPPORTED = 8  /* valid request that this build cannot run           */
+} tf_status;
+
+typedef enum tf_dtype { TF_F16 = 0, TF_BF16 = 1, TF_F32 = 2, TF_U8 = 3 } tf_dtype;
+
+/* Regime selector for tf_qlinear_ex. */
+typedef enum tf_regime {
+  TF_REGIME_AUTO = 0,  /* pick by M and shape (what tf_qlinear does)            */
+  TF_REGIME_GEMV = 1,  /* decode: TMA-streamed split-K int4 GEMV, M <= 32       */
+  TF_REGIME_GEMM = 2,  /* prefill: TMA + tcgen05/TMEM GEMM, dequant once in smem */
+  TF_REGIME_SIMT = 3   /* any shape/alignment: CUDA-core kernel                  */
+} tf_regime;
+
+/* ABI version of this header (bumped on any signature change). */
+int tf_abi_version(void);
+/* Static text for a status code. */
+const char* tf_status_string(int status);
+/* Thread-local detail of the last failure reported by this library. */
+const char* tf_last_error_message(void);
+
+/* ---- quantized_linear -------------------------------------------------
+ * Replaces `tritonforge.kernels.quantized_linear`
+ * (reference src/tritonforge/kernels/dequant_gemm.py:151-210, validation
+ * :121-148, Triton kernel :39-113):
+ *   out[M, N] = x[M, K] @ dequant(packed)[:K] (+ bias)
+ * x holds M rows of K values with row stride `ldx` elements; columns
+ * K..K_pad-1 are treated as zero (the reference zero-pads x, :166-167).
+ * Weights are dequantised and rounded to the activation dtype, products are
+ * accumulated in fp32, the result is rounded to the activation dtype and the
+ * bias (any of fp16/bf16/fp32, or NULL) is added and rounded again -- the
+ * rounding points of the reference oracle (reference.py:21-36).
+ * `workspace` must hold tf_qlinear_workspace_bytes(...) bytes and be zeroed
+ * once before its first use; calls leave it zeroed. Calls that share a
+ * workspace must be ordered on one stream.
+ */
+size_t tf_qlinear_workspace_bytes(int64_t M, int64_t N, int64_t K_pad, int32_t group_size);
+
+int tf_qlinear(const void* x, int64_t ldx, int x_dtype,
+               const uint8_t* packed, const void* scales, const void* zeros, int param_dtype,
+               const void* bias, int bias_dtype,
+               void* out, int64_t ldo,
+               int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as tf_qlinear with an explicit regime (tf_regime); used by tests and
+ * benchmarks to exercise each kernel. AUTO behaves exactly like tf_qlinear. */
+int tf_qlinear_ex(const void* x, int64_t ldx, int x_dtype,
+                  const uint8_t* packed, const void* scales, const void* zeros, int param_dtype,
+                  const void* bias, int bias_dtype,
+                  void* out, int64_t ldo,
+                  int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                  void* workspace, size_t workspace_bytes, int regime, void* stream);
+
+/* Reads the device-side error word of a workspace (blocking copy on `stream`):
+ * 0 when every kernel that used it completed its bounded waits. */
+int tf_workspace_error(const void* workspace, int* error_out, void* stream);
+
+/* ---- rmsnorm_residual / rmsnorm ---------------------------------------
+ * Replaces `tritonforge.kernels.rmsnorm_residual` and `.rmsnorm`
+ * (reference src/tritonforge/kernels/rmsnorm_residual.py:141-161, launch
+ * :85-138, kernel :26-79; oracle reference.py:39-50):
+ *   summed = x + residual                     (rounded to dtype)
+ *   normed = (summed * rsqrt(mean(summed^2) + eps)) -> dtype, * weight -> dtype
+ * `residual == NULL` gives plain RMSNorm (then `summed` must be NULL);
+ * `summed == NULL` skips writing the sum. x, residual, normed and summed are
+ * [M, N] contiguous of `dtype`; weight is [N] of `w_dtype`.
+ */
+int tf_rmsnorm_residual(const void* x, const void* residual, const void* weight, int w_dtype,
+                        void* normed, void* summed, int64_t M, int64_t N, float eps,
+                        int dtype, void* stream);
+
+/* ---- swiglu -------------------------------------------------------------
+ * Replaces `tritonforge.kernels.swiglu` (reference src/tritonforge/kernels/
+ * swiglu.py:36-57, kernel :21-30; oracle reference.py:53-57):
+ *   out = (gate * sigmoid(gate)) * up, in fp32, rounded once to dtype,
+ * over `numel` contiguous elements.
+ */
+int tf_swiglu(const void* gate, const void* up, void* out, int64_t numel, int dtype,
+              void* stream);
+
+/* ---- quantizer and format helpers ---------------------------------------
+ * tf_quantize_int4 replaces `tritonforge.quant.quantize_int4_group`
+ * (reference src/tritonforge/quant.py:29-63), bit-exact: w is the fp32
+ * [N, K] weight (nn.Linear layout); outputs are packed [K_pad/2, N] and
+ * scales/zeros [K_pad/g, N] of `param_dtype`, K_pad = ceil(K/g)*g.
+ * tf_dequantize_int4 replaces `quant.dequantize_int4` (quant.py:90-105):
+ * out [K_pad, N] of `out_dtype` = ((code - zero) * scale) in fp32, rounded.
+ * tf_unpack_int4 replaces `quant.unpack_int4` (quant.py:66-74): codes
+ * uint8 [K_pad, N].
+ */
+int tf_quantize_int4(const float* w, int64_t N, int64_t K, int32_t group_size,
+                     uint8_t* packed, void* scales, void* zeros, int param_dtype,
+                     void* stream);
+
+int tf_dequantize_int4(const uint8_t* packed, const void* scales, const void* zeros,
+                       int param_dtype, void* out, int out_dtype,
+                       int64_t K_pad, int64_t N, int32_t group_size, void* stream);
+
+int tf_unpack_int4(const uint8_t* packed, uint8_t* codes, int64_t K_pad, int64_t N,
+                   void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* TRITONFORGE_B200_H */

@@ -1,0 +1,56 @@
+"""Parity helpers: compare CUDA outputs with the CPU oracle.
+
+Tolerance (the contract for floating-point outputs): max-abs error
+<= 1e-2 x RMS(oracle output) for fp16 and <= 2e-2 x RMS for bf16. Integer and
+byte outputs (codes, packed nibbles, scale/zero bit patterns) must be equal.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import ops as oops
+from oracle import quant as oquant
+
+RMS_TOL = {torch.float16: 1e-2, torch.bfloat16: 2e-2, torch.float32: 1e-5}
+NP_DT = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, what: str = "",
+                     max_mismatch: float | None = None) -> dict:
+    got = f32(out)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    if got.size == 0:
+        return {"max_abs": 0.0, "rms": 0.0}
+    err = float(np.max(np.abs(got.astype(np.float64) - ref.astype(np.float64))))
+    rms = oops.rms(ref)
+    tol = RMS_TOL[dtype] * rms
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    assert err <= tol, f"{what}: max-abs {err:.4g} > {RMS_TOL[dtype]} x RMS {rms:.4g}"
+    mism = float(np.mean(got != ref))
+    if max_mismatch is not None:
+        assert mism <= max_mismatch, f"{what}: {mism:.3%} of elements differ from the oracle"
+    return {"max_abs": err, "rms": rms, "mismatch": mism}
+
+
+def oracle_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+                  bias: torch.Tensor | None, group: int = 128) -> np.ndarray:
+    return oops.quantized_linear(f32(x), packed.cpu().numpy(), f32(scales), f32(zeros),
+                                 None if bias is None else f32(bias), group, NP_DT[x.dtype])
+
+
+def oracle_quantize(w: torch.Tensor, group: int, dtype: torch.dtype):
+    return oquant.quantize_int4_group(w.detach().float().cpu().numpy(), group, NP_DT[dtype])

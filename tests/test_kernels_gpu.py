@@ -1,0 +1,249 @@
+"""GPU parity: every CUDA kernel against the CPU oracle on identical seeded
+inputs (shapes of the reference's own tests, of the 0.5B/7B/72B configurations,
+and the edge cases), plus the committed golden vectors of the reference."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as oops
+from oracle import quant as oquant
+from tests import golden_io as gio
+from tests.parity import NP_DT, assert_rms_close, bits, f32, oracle_linear, oracle_quantize
+from tritonforge_b200 import _lib, kernels, quant
+
+pytestmark = pytest.mark.gpu
+GROUP = 128
+DTYPES = [torch.float16, torch.bfloat16]
+
+
+def _linear_inputs(m, n, k, dtype, w_std=1.0, bias=True, seed=0, param_dtype=None):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g).to(dtype).cuda()
+    w = (torch.randn(n, k, generator=g) * w_std).cuda()
+    packed, scales, zeros, _ = quant.quantize_int4_group(w, GROUP, param_dtype or dtype)
+    b = torch.randn(n, generator=g).to(dtype).cuda() if bias else None
+    return x, packed, scales, zeros, b
+
+
+# ---- quantized_linear ------------------------------------------------------
+REF_SHAPES = [(1, 64, 128), (1, 896, 896), (3, 127, 129), (16, 128, 256), (17, 64, 256),
+              (64, 512, 896), (128, 256, 1024)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", REF_SHAPES)
+def test_quantized_linear_reference_shapes(m, n, k, dtype):
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b)
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, dtype, f"qlinear {m}x{n}x{k}", max_mismatch=0.02)
+
+
+DECODE_SHAPES = [(896, 4864), (4864, 896), (896, 896), (896, 128),
+                 (3584, 3584), (3584, 512), (3584, 18944), (18944, 3584)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("k,n", DECODE_SHAPES)
+@pytest.mark.parametrize("m", [1, 4, 8, 16, 32])
+def test_gemv_decode_shapes(m, k, n, dtype):
+    if m in (4, 32) and n * k > 30_000_000:
+        pytest.skip("covered by the other M values at this size")
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, bias=(n != 512), seed=m + n)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemv"})
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, dtype, f"gemv {m}x{n}x{k}", max_mismatch=0.02)
+
+
+@pytest.mark.parametrize("regime", ["gemv", "simt"])
+@pytest.mark.parametrize("xdt,pdt", [(torch.bfloat16, torch.float16), (torch.float16, torch.bfloat16)])
+def test_mixed_param_dtype(regime, xdt, pdt):
+    # the reference's QuantLinear stores fp16 scales by default, also for bf16 models
+    x, packed, scales, zeros, b = _linear_inputs(8, 4864, 896, xdt, w_std=0.02, param_dtype=pdt)
+    b = b.to(pdt)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": regime})
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, xdt, "mixed", max_mismatch=0.02)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", [(1, 4864, 896), (5, 896, 4864), (32, 512, 3584), (8, 256, 200),
+                                   (3, 127, 129), (40, 4864, 896)])
+def test_simt_regime(m, n, k, dtype):
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, seed=7)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "simt"})
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, dtype, "simt", max_mismatch=0.02)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_gemv_x_shorter_than_packed_k(dtype):
+    # K=200 < K_pad=256: the kernel reads x[:, 200:] as zeros (reference pads x)
+    x, packed, scales, zeros, b = _linear_inputs(4, 1024, 200, dtype, w_std=0.02, seed=3)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemv"})
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, dtype, "gemv K<K_pad", max_mismatch=0.02)
+
+
+def test_no_bias_fp32_bias_and_strided_x():
+    x, packed, scales, zeros, _ = _linear_inputs(4, 2048, 1024, torch.float16, w_std=0.02, seed=5)
+    ref = oracle_linear(x, packed, scales, zeros, None)
+    assert_rms_close(kernels.quantized_linear(x, packed, scales, zeros), ref, torch.float16, "no bias")
+    b32 = torch.randn(2048, device="cuda")
+    ref_b = oops.quantized_linear(f32(x), packed.cpu().numpy(), f32(scales), f32(zeros), f32(b32), GROUP,
+                                  "float16")
+    assert_rms_close(kernels.quantized_linear(x, packed, scales, zeros, b32), ref_b, torch.float16, "f32 bias")
+    wide = torch.zeros(4, 1536, dtype=torch.float16, device="cuda")
+    wide[:, :1024] = x
+    out = kernels.quantized_linear(wide[:, :1024], packed, scales, zeros)  # row stride 1536
+    assert_rms_close(out, ref, torch.float16, "strided x", max_mismatch=0.02)
+
+
+def test_empty_and_determinism():
+    x, packed, scales, zeros, b = _linear_inputs(0, 512, 256, torch.float16)
+    assert kernels.quantized_linear(x, packed, scales, zeros, b).shape == (0, 512)
+    x, packed, scales, zeros, b = _linear_inputs(16, 3584, 18944, torch.bfloat16, w_std=0.02, seed=9)
+    a1 = kernels.quantized_linear(x, packed, scales, zeros, b)
+    a2 = kernels.quantized_linear(x, packed, scales, zeros, b)
+    assert torch.equal(a1.view(torch.int16), a2.view(torch.int16)), "split-K reduction is not deterministic"
+    ws = _lib.workspaces.get(x.device, 0)
+    err = _lib.ctypes.c_int(0)
+    rc = _lib.load().tf_workspace_error(ws.data_ptr(), _lib.ctypes.byref(err),
+                                        _lib.stream_ptr(x.device))
+    assert rc == 0 and err.value == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_large_m_rows_sampled(dtype):
+    # prefill shape of the 7B config: check 64 sampled rows against the oracle
+    m, k, n = 2048, 3584, 3584
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, seed=11)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b)
+    rows = torch.randperm(m, generator=torch.Generator().manual_seed(0))[:64].sort().values
+    ref = oracle_linear(x[rows.cuda()], packed, scales, zeros, b)
+    assert_rms_close(out[rows.cuda()], ref, dtype, "prefill rows", max_mismatch=0.02)
+
+
+def test_golden_linear_cases():
+    rec = gio.load()
+    for case in rec["linear/cases"]:
+        case = str(case)
+        dt = torch.float16 if gio.dtype_of(rec, f"{case}/x") == "float16" else torch.bfloat16
+        x = torch.from_numpy(gio.get_f32(rec, f"{case}/x")).to(dt).cuda()
+        packed = torch.from_numpy(gio.get(rec, f"{case}/packed")[0]).cuda()
+        s = torch.from_numpy(gio.get_f32(rec, f"{case}/scales")).to(dt).cuda()
+        z = torch.from_numpy(gio.get_f32(rec, f"{case}/zeros")).to(dt).cuda()
+        b = (torch.from_numpy(gio.get_f32(rec, f"{case}/bias")).to(dt).cuda()
+             if gio.has(rec, f"{case}/bias") else None)
+        out = kernels.quantized_linear(x, packed, s, z, b)
+        assert_rms_close(out, gio.get_f32(rec, f"{case}/out"), dt, case, max_mismatch=0.05)
+
+
+# ---- rmsnorm_residual / rmsnorm ---------------------------------------------
+NORM_SHAPES = [(1, 896), (4, 896), (16, 1536), (128, 896), (1, 3584), (64, 3584), (2048, 3584),
+               (1, 8192), (3, 100), (2, 16384), (1, 65544)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n", NORM_SHAPES)
+def test_rmsnorm_residual(m, n, dtype):
+    g = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, n, generator=g).to(dtype).cuda()
+    r = torch.randn(m, n, generator=g).to(dtype).cuda()
+    w = (1 + 0.02 * torch.randn(n, generator=g)).to(dtype).cuda()
+    normed, summed = kernels.rmsnorm_residual(x, r, w)
+    ref_n, ref_s = oops.rmsnorm_residual(f32(x), f32(r), f32(w), 1e-6, NP_DT[dtype])
+    assert np.array_equal(f32(summed), ref_s), "summed must equal round(x + r) exactly"
+    assert_rms_close(normed, ref_n, dtype, "normed", max_mismatch=0.01)
+    plain = kernels.rmsnorm(x, w)
+    assert_rms_close(plain, oops.rmsnorm(f32(x), f32(w), 1e-6, NP_DT[dtype]), dtype, "plain",
+                     max_mismatch=0.01)
+
+
+def test_rmsnorm_golden():
+    rec = gio.load()
+    for case in rec["rmsnorm/cases"]:
+        case = str(case)
+        dt = torch.float16 if gio.dtype_of(rec, f"{case}/x") == "float16" else torch.bfloat16
+        t = {k: torch.from_numpy(gio.get_f32(rec, f"{case}/{k}")).to(dt).cuda() for k in "xrw"}
+        normed, summed = kernels.rmsnorm_residual(t["x"], t["r"], t["w"])
+        assert np.array_equal(bits(summed), gio.get(rec, f"{case}/summed")[0])
+        assert_rms_close(normed, gio.get_f32(rec, f"{case}/normed"), dt, case, max_mismatch=0.02)
+        assert_rms_close(kernels.rmsnorm(t["x"], t["w"]), gio.get_f32(rec, f"{case}/plain"), dt, case)
+
+
+# ---- swiglu -------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float32])
+@pytest.mark.parametrize("shape", [(1, 4864), (3, 127), (16, 4864), (129, 4864), (64, 18944), (7,)])
+def test_swiglu(shape, dtype):
+    g = torch.Generator().manual_seed(sum(shape))
+    gate = (torch.randn(*shape, generator=g) * 3).to(dtype).cuda()
+    up = torch.randn(*shape, generator=g).to(dtype).cuda()
+    out = kernels.swiglu(gate, up)
+    ref = oops.swiglu(f32(gate), f32(up), NP_DT[dtype])
+    assert_rms_close(out, ref, dtype, "swiglu", max_mismatch=0.01 if dtype != torch.float32 else None)
+
+
+def test_swiglu_unaligned_and_golden():
+    base_g = torch.randn(4097, dtype=torch.float16, device="cuda")
+    base_u = torch.randn(4097, dtype=torch.float16, device="cuda")
+    gate, up = base_g[1:], base_u[1:]  # 2-byte offset: scalar path
+    ref = oops.swiglu(f32(gate), f32(up), "float16")
+    assert_rms_close(kernels.swiglu(gate, up), ref, torch.float16, "unaligned", max_mismatch=0.01)
+    rec = gio.load()
+    for case in rec["swiglu/cases"]:
+        case = str(case)
+        dt = torch.float16 if gio.dtype_of(rec, f"{case}/g") == "float16" else torch.bfloat16
+        gg = torch.from_numpy(gio.get_f32(rec, f"{case}/g")).to(dt).cuda()
+        uu = torch.from_numpy(gio.get_f32(rec, f"{case}/u")).to(dt).cuda()
+        assert_rms_close(kernels.swiglu(gg, uu), gio.get_f32(rec, f"{case}/out"), dt, case,
+                         max_mismatch=0.01)
+
+
+# ---- quantizer / unpack / dequant: bit-exact ------------------------------------
+def test_quantizer_golden_bit_exact():
+    rec = gio.load()
+    for case in rec["quant/cases"]:
+        p = f"quant/{case}"
+        n, k, g, k_pad, is_bf16 = (int(v) for v in rec[f"{p}/meta"])
+        dt = torch.bfloat16 if is_bf16 else torch.float16
+        w = torch.from_numpy(gio.get(rec, f"{p}/w")[0]).cuda()
+        packed, scales, zeros, kp = quant.quantize_int4_group(w, g, dt)
+        assert kp == k_pad
+        assert np.array_equal(packed.cpu().numpy(), gio.get(rec, f"{p}/packed")[0]), case
+        assert np.array_equal(bits(scales), gio.get(rec, f"{p}/scales")[0]), case
+        assert np.array_equal(bits(zeros), gio.get(rec, f"{p}/zeros")[0]), case
+        assert np.array_equal(quant.unpack_int4(packed).cpu().numpy(), gio.get(rec, f"{p}/codes")[0])
+        dense = quant.dequantize_int4(packed, scales, zeros, g, dt)
+        assert np.array_equal(bits(dense), gio.get(rec, f"{p}/dense")[0]), case
+
+
+@pytest.mark.parametrize("n,k,group,dtype,std", [
+    (4864, 896, 128, torch.float16, 0.02), (896, 4864, 128, torch.bfloat16, 0.02),
+    (1000, 300, 64, torch.float16, 1.0), (77, 1000, 256, torch.bfloat16, 0.5),
+    (33, 130, 2, torch.float16, 1.0), (64, 96, 6, torch.float16, 1.0), (130, 1024, 512, torch.float16, 3.0)])
+def test_quantizer_bit_exact_vs_oracle(n, k, group, dtype, std):
+    w = torch.randn(n, k, generator=torch.Generator().manual_seed(n * k)) * std
+    w[0, :group] = 0.0          # all-zero group: zero-point -0.0
+    w[1, :] = 0.25              # constant row
+    packed, scales, zeros, k_pad = quant.quantize_int4_group(w.cuda(), group, dtype)
+    o_packed, o_scales, o_zeros, o_kpad = oracle_quantize(w, group, dtype)
+    assert k_pad == o_kpad
+    assert np.array_equal(packed.cpu().numpy(), o_packed)
+    assert np.array_equal(bits(scales), o_scales)
+    assert np.array_equal(bits(zeros), o_zeros)
+    dense = quant.dequantize_int4(packed, scales, zeros, group, dtype)
+    o_dense = oquant.dequantize_int4(o_packed, o_scales, o_zeros, group, NP_DT[dtype], NP_DT[dtype])
+    assert np.array_equal(bits(dense), o_dense)
+
+
+def test_quantize_cpu_input_round_trip_device():
+    w = torch.randn(64, 256)
+    packed, scales, zeros, _ = quant.quantize_int4_group(w, 128)
+    assert packed.device.type == "cpu" and scales.device.type == "cpu"
+    recon = quant.quantize_dequantize(w.cuda(), group_size=128)
+    err = quant.quantization_error(w.cuda(), recon)
+    assert err["max_abs"] < 0.3 and err["mean_abs"] < 0.12  # reference tests/test_quant.py:30-36

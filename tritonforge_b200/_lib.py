@@ -1,0 +1,144 @@
+"""Loader for the native library ``libtritonforge_b200.so`` (C ABI in
+``include/tritonforge_b200.h``) and the glue the Python API shares: dtype codes,
+status checking, per-device workspaces and the current CUDA stream.
+
+There is no CPU fallback: every op runs the CUDA kernels in this library, and
+importing an op without the built library raises immediately.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import threading
+
+import torch
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libtritonforge_b200.so"
+
+# tf_dtype
+F16, BF16, F32, U8 = 0, 1, 2, 3
+# tf_regime
+REGIME_AUTO, REGIME_GEMV, REGIME_GEMM, REGIME_SIMT = 0, 1, 2, 3
+REGIMES = {"auto": REGIME_AUTO, "gemv": REGIME_GEMV, "gemm": REGIME_GEMM, "simt": REGIME_SIMT}
+
+# tf_status
+OK = 0
+ERR_BAD_SHAPE, ERR_BAD_DTYPE, ERR_UNALIGNED, ERR_CUDA, ERR_TIMEOUT = 1, 2, 3, 4, 5
+ERR_WORKSPACE, ERR_BAD_ARG, ERR_UNSUPPORTED = 6, 7, 8
+
+_DT = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32, torch.uint8: U8}
+
+_vp, _i64, _i32, _sz, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/tritonforge_b200.h
+SIGNATURES = {
+    "tf_abi_version": (_i32, []),
+    "tf_status_string": (ctypes.c_char_p, [_i32]),
+    "tf_last_error_message": (ctypes.c_char_p, []),
+    "tf_qlinear_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
+    "tf_qlinear": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
+                          _i64, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
+    "tf_qlinear_ex": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
+                             _i64, _i64, _i64, _i64, _i32, _vp, _sz, _i32, _vp]),
+    "tf_workspace_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
+    "tf_rmsnorm_residual": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _f32, _i32, _vp]),
+    "tf_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp]),
+    "tf_quantize_int4": (_i32, [_vp, _i64, _i64, _i32, _vp, _vp, _vp, _i32, _vp]),
+    "tf_dequantize_int4": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i32, _vp]),
+    "tf_unpack_int4": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+}
+
+_lib: ctypes.CDLL | None = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = os.environ.get("TRITONFORGE_B200_LIB", str(LIB_PATH))
+            if not pathlib.Path(path).exists():
+                raise RuntimeError(
+                    f"tritonforge_b200 native library not found at {path}; build it with "
+                    "`make -C tritonforge_b200/csrc` (or __graft_entry__.build())")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def check(rc: int, what: str) -> None:
+    if rc != OK:
+        lib = load()
+        msg = lib.tf_last_error_message().decode(errors="replace")
+        status = lib.tf_status_string(rc).decode()
+        raise RuntimeError(f"{what} failed: {status} ({rc}): {msg}")
+
+
+def require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    """All given tensors must live on one CUDA device; returns it."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "tritonforge_b200 ops run on CUDA only (got a tensor on "
+                f"{t.device}); there is no CPU implementation")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    if dev is None:
+        raise RuntimeError("no CUDA tensor given")
+    return dev
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class _Workspaces:
+    """Per-device zero-initialised scratch for split-K partials and tickets.
+
+    Kernels leave their ticket counters at zero, so a buffer is zeroed only when
+    it is (re)allocated. Reallocation happens outside any CUDA-graph capture:
+    callers that capture size it first with ``reserve``.
+    """
+
+    def __init__(self) -> None:
+        self._bufs: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        buf = self._bufs.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 20, 0 if buf is None else 2 * buf.numel())
+            buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+            self._bufs[idx] = buf
+        return buf
+
+    def reserve(self, device: torch.device, nbytes: int) -> None:
+        self.get(device, nbytes)
+
+
+workspaces = _Workspaces()

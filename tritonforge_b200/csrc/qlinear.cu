@@ -1,0 +1,91 @@
+// tf_qlinear: argument validation (mirrors the reference's `_validate`,
+// src/tritonforge/kernels/dequant_gemm.py:121-148) and regime dispatch:
+//   M <= 32 and TMA-compatible shapes -> decode GEMV (qlinear_gemv.cu)
+//   larger M and tcgen05-compatible   -> prefill GEMM (qlinear_tc.cu)
+//   anything else                     -> CUDA-core kernel (qlinear_simt.cu)
+#include "qlinear.cuh"
+
+namespace tf {
+namespace {
+
+bool is_half(int dt) { return dt == TF_F16 || dt == TF_BF16; }
+bool is_param(int dt) { return dt == TF_F16 || dt == TF_BF16 || dt == TF_F32; }
+
+int validate(const QLinearProblem& pb) {
+  if (!is_half(pb.x_dtype)) return fail(TF_ERR_BAD_DTYPE, "qlinear: x dtype must be fp16/bf16 (got %d)", pb.x_dtype);
+  if (!is_param(pb.param_dtype))
+    return fail(TF_ERR_BAD_DTYPE, "qlinear: scales/zeros dtype must be fp16/bf16/fp32 (got %d)", pb.param_dtype);
+  if (pb.bias && !is_param(pb.bias_dtype))
+    return fail(TF_ERR_BAD_DTYPE, "qlinear: bias dtype must be fp16/bf16/fp32 (got %d)", pb.bias_dtype);
+  if (pb.M < 0 || pb.N < 0 || pb.K < 0 || pb.K_pad < 0)
+    return fail(TF_ERR_BAD_SHAPE, "qlinear: negative shape");
+  if (pb.group_size < 2 || pb.group_size % 2 != 0)
+    return fail(TF_ERR_BAD_ARG, "qlinear: group_size must be an even number >= 2 (got %d)", pb.group_size);
+  if (pb.K_pad % pb.group_size != 0)
+    return fail(TF_ERR_BAD_SHAPE, "qlinear: packed K=%lld not a multiple of group_size=%d", (long long)pb.K_pad,
+                pb.group_size);
+  if (pb.K > pb.K_pad)
+    return fail(TF_ERR_BAD_SHAPE, "qlinear: x has K=%lld > packed K=%lld", (long long)pb.K, (long long)pb.K_pad);
+  if (pb.ldx < pb.K || pb.ldo < pb.N) return fail(TF_ERR_BAD_SHAPE, "qlinear: leading dimension too small");
+  if (pb.M == 0 || pb.N == 0) return TF_OK;
+  if (!pb.out || !pb.packed || !pb.scales || !pb.zeros || (pb.K > 0 && !pb.x))
+    return fail(TF_ERR_BAD_ARG, "qlinear: null pointer");
+  return TF_OK;
+}
+
+}  // namespace
+}  // namespace tf
+
+extern "C" size_t tf_qlinear_workspace_bytes(int64_t M, int64_t N, int64_t K_pad, int32_t group_size) {
+  (void)group_size;
+  size_t a = tf::gemv_workspace_bytes(M, N, K_pad);
+  size_t b = tf::gemm_workspace_bytes(M, N, K_pad);
+  return a > b ? a : b;
+}
+
+extern "C" int tf_qlinear_ex(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
+                             const void* zeros, int param_dtype, const void* bias, int bias_dtype, void* out,
+                             int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                             void* workspace, size_t workspace_bytes, int regime, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,         x_dtype, packed, scales,    zeros,          param_dtype,
+                    bias, bias_dtype,  out,     ldo,    M,         N,              K,
+                    K_pad, group_size, workspace, workspace_bytes};
+  int rc = validate(pb);
+  if (rc != TF_OK || M == 0 || N == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (regime) {
+    case TF_REGIME_AUTO:
+      if (gemv_supported(pb)) return gemv_launch(pb, st);
+      if (gemm_supported(pb)) return gemm_launch(pb, st);
+      return simt_launch(pb, st);
+    case TF_REGIME_GEMV:
+      if (!gemv_supported(pb)) return fail(TF_ERR_UNSUPPORTED, "qlinear: GEMV regime cannot take this problem");
+      return gemv_launch(pb, st);
+    case TF_REGIME_GEMM:
+      if (!gemm_supported(pb)) return fail(TF_ERR_UNSUPPORTED, "qlinear: GEMM regime cannot take this problem");
+      return gemm_launch(pb, st);
+    case TF_REGIME_SIMT:
+      return simt_launch(pb, st);
+    default:
+      return fail(TF_ERR_BAD_ARG, "qlinear: unknown regime %d", regime);
+  }
+}
+
+extern "C" int tf_qlinear(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
+                          const void* zeros, int param_dtype, const void* bias, int bias_dtype, void* out,
+                          int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  return tf_qlinear_ex(x, ldx, x_dtype, packed, scales, zeros, param_dtype, bias, bias_dtype, out, ldo, M, N, K,
+                       K_pad, group_size, workspace, workspace_bytes, TF_REGIME_AUTO, stream);
+}
+
+extern "C" int tf_workspace_error(const void* workspace, int* error_out, void* stream) {
+  using namespace tf;
+  if (!workspace || !error_out) return fail(TF_ERR_BAD_ARG, "workspace_error: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(error_out, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return check_launch("workspace_error copy");
+  if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("workspace_error sync");
+  return *error_out ? TF_ERR_TIMEOUT : TF_OK;
+}

@@ -1,0 +1,39 @@
+// Problem description shared by the quantized-linear kernels and dispatcher.
+#pragma once
+
+#include "common.cuh"
+
+namespace tf {
+
+// Workspace header: [0, 4) device error word (bounded-wait expiry bits).
+constexpr size_t kWsHeader = 256;
+
+struct QLinearProblem {
+  const void* x;
+  int64_t ldx;
+  int x_dtype;
+  const uint8_t* packed;
+  const void* scales;
+  const void* zeros;
+  int param_dtype;
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int64_t ldo;
+  int64_t M, N, K, K_pad;
+  int group_size;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+bool gemv_supported(const QLinearProblem& pb);
+size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
+int gemv_launch(const QLinearProblem& pb, cudaStream_t st);
+
+bool gemm_supported(const QLinearProblem& pb);
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
+int gemm_launch(const QLinearProblem& pb, cudaStream_t st);
+
+int simt_launch(const QLinearProblem& pb, cudaStream_t st);
+
+}  // namespace tf
