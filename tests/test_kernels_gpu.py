@@ -80,12 +80,13 @@ def test_simt_regime(m, n, k, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-def test_gemv_x_shorter_than_packed_k(dtype):
-    # K=200 < K_pad=256: the kernel reads x[:, 200:] as zeros (reference pads x)
-    x, packed, scales, zeros, b = _linear_inputs(4, 1024, 200, dtype, w_std=0.02, seed=3)
-    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemv"})
+@pytest.mark.parametrize("k,regime", [(192, "gemv"), (200, "auto"), (1168, "gemv")])
+def test_x_shorter_than_packed_k(k, regime, dtype):
+    # K < K_pad: the kernels read x[:, K:] as zeros (the reference pads x)
+    x, packed, scales, zeros, b = _linear_inputs(4, 1024, k, dtype, w_std=0.02, seed=3)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": regime})
     ref = oracle_linear(x, packed, scales, zeros, b)
-    assert_rms_close(out, ref, dtype, "gemv K<K_pad", max_mismatch=0.02)
+    assert_rms_close(out, ref, dtype, f"K={k} < K_pad", max_mismatch=0.02)
 
 
 def test_no_bias_fp32_bias_and_strided_x():

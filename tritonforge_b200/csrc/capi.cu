@@ -82,6 +82,22 @@ int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void
   return TF_OK;
 }
 
+int encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                         const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
+                         CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TF_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), d, s, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TF_ERR_BAD_ARG, "cuTensorMapEncodeTiled(3d) failed (%d)", (int)r);
+  return TF_OK;
+}
+
 }  // namespace tf
 
 extern "C" {

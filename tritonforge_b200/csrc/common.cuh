@@ -133,6 +133,16 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// 3-D tiled TMA load (no multicast), completion signalled on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned, size multiple of 16).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -170,5 +180,8 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint3
 int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                          uint64_t dim0, uint64_t dim1, uint64_t stride1_bytes,
                          uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle);
+int encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                         const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
+                         CUtensorMapSwizzle swizzle);
 
 }  // namespace tf

@@ -5,7 +5,8 @@
 
 namespace tf {
 
-// Workspace header: [0, 4) device error word (bounded-wait expiry bits).
+// Workspace layout: [0, 256) header, word 0 = device error bits of bounded
+// waits. The kernels keep all other scratch on chip.
 constexpr size_t kWsHeader = 256;
 
 struct QLinearProblem {

@@ -4,59 +4,79 @@
 // (src/tritonforge/kernels/dequant_gemm.py:39-113) for small M, where the op is
 // bound by streaming the packed weights from HBM.
 //
-// Structure (one CTA = WN consumer warps + 1 producer warp):
-//  * A CTA owns 128*WN output columns and a contiguous range of 128-k stages
-//    (split-K across CTAs, grid = [column blocks, ksplit]).
-//  * The producer warp streams, per stage, through TMA into a ring of S
-//    shared-memory stages: the packed tile [64 rows x 128 B] per consumer warp
-//    (128-byte swizzle), the x slice as 8 boxes [M_pad x 16 k] and the group's
-//    scales/zeros (1-D bulk copies). Weights carry an L2 evict-first hint.
+// Structure (one CTA = WK consumer warps + 1 producer warp, 128 output columns):
+//  * Work unit = a stage of 256 k (two 128-k groups). Grid = [N/128 column
+//    blocks, ksplit]; a CTA owns a contiguous range of stages of its column
+//    block. Consumer warps work in pairs: pair p takes every (WK/2)-th stage
+//    and each warp of the pair one of its two groups, so every warp processes
+//    whole groups and the stages of a CTA are consumed concurrently.
+//  * The producer issues 4 TMA operations per stage (the per-SM TMA engine is
+//    limited by operations in flight, so each carries as many bytes as
+//    possible): the packed tile [128 rows x 128 B] (16 KiB, 128-byte swizzle,
+//    L2 evict-first), the x slice [M_pad x 256 k] as one 3-D box laid out
+//    [16-k chunk][row][16 k] (conflict-free B-fragment reads), and the two
+//    scale/zero rows of the stage.
 //  * Consumer warps dequantise in registers with the reference's rounding:
 //    w = round_x((code - zero) * scale). Nibbles become halves with one lop3
 //    against a magic exponent (1024+c / 64+c for fp16, 128+c for bf16); the
 //    subtraction is exact and `mul.rn` rounds once, so every dequantised
 //    weight equals the oracle's bit for bit.
-//  * The dot products run on the tensor pipe with mma.sync m16n8k16: the
-//    dequantised weights are the A operand (16 output columns x 16 k), x^T is
-//    B (16 k x 8 tokens), fp32 accumulators. The k order inside each 16-k
-//    step is permuted identically for A and B so that one byte pair from two
-//    packed rows fills one A register (no shuffles).
-//  * Split-K partials go to a fp32 workspace; the last CTA of a column block
-//    (atomic ticket) sums them in split order (deterministic), rounds, adds the
-//    bias, rounds again (reference.py:33-35) and resets its ticket.
+//  * Dot products run on the tensor pipe with mma.sync m16n8k16: dequantised
+//    weights are the A operand (16 output columns x 16 k), x^T is B (16 k x 8
+//    tokens), fp32 accumulators. The k order inside each 16-k step is permuted
+//    identically for A and B so one byte pair from two packed rows fills one A
+//    register without shuffles.
+//  * Reduction: the warps' partial sums are added in shared memory (fixed
+//    order); the ksplit CTAs of a column block form a thread-block cluster and
+//    add their partials through distributed shared memory (fixed rank order),
+//    so results are deterministic and no global scratch is used. Each rank
+//    rounds, adds the bias and rounds again (reference.py:33-35) for its slice
+//    of the columns.
 // Every mbarrier wait is bounded (1 s); on expiry the kernel records an error
-// bit in the workspace header and drains its own in-flight copies.
+// bit in the workspace header, drains its own in-flight copies and finishes.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "qlinear.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tf {
 namespace gemv {
 
-constexpr int kRowsPerStage = 64;  // packed rows (128 k) per stage
-constexpr int kWarpCols = 128;     // output columns per consumer warp
-constexpr int kWBoxBytes = kRowsPerStage * kWarpCols;  // 8 KiB
+constexpr int kCols = 128;                 // output columns per CTA
+constexpr int kStageK = 256;               // k per stage (two groups of 128)
+constexpr int kWRows = kStageK / 2;        // packed rows per stage
+constexpr int kWBoxBytes = kWRows * kCols; // 16 KiB
+constexpr int kMaxCluster = 8;
 
-__host__ __device__ constexpr int x_bytes(int nt) { return 8 * (8 * nt) * 32; }
-__host__ __device__ constexpr int stage_bytes(int wn, int nt) {
-  return ((wn * kWBoxBytes + x_bytes(nt) + 2 * wn * kWarpCols * 2) + 1023) / 1024 * 1024;
+__host__ __device__ constexpr int warps_k(int nt) { return 4; }
+__host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 4 ? 1 : 2; }
+constexpr int kPairs = 2;  // consumer warp pairs per CTA (warps_k / 2)
+__host__ __device__ constexpr int x_chunk_bytes(int nt) { return 8 * nt * 32; }  // one 16-k chunk, all rows
+__host__ __device__ constexpr int x_off() { return kWBoxBytes; }
+__host__ __device__ constexpr int s_off(int nt) { return x_off() + 16 * x_chunk_bytes(nt); }
+__host__ __device__ constexpr int z_off(int nt) { return s_off(nt) + 2 * kCols * 2; }
+__host__ __device__ constexpr int stage_tx_bytes(int nt) { return z_off(nt) + 2 * kCols * 2; }
+__host__ __device__ constexpr int stage_bytes(int nt) { return (stage_tx_bytes(nt) + 1023) / 1024 * 1024; }
+constexpr int kRedPitch = kCols + 4;       // floats per row of the smem reduction tiles
+__host__ __device__ constexpr int red_bytes(int nt) {
+  return (warps_k(nt) + 1) * 8 * nt * kRedPitch * 4;  // per-warp tiles + the CTA tile
 }
 
 struct Args {
-  const void* scales;
-  const void* zeros;
   const void* bias;
   void* out;
-  float* partials;
-  int* tickets;
   int* err;
   int64_t ldo;
   int M, N;
-  int n_stages;        // K_pad / 128
+  int n_stages;         // ceil(K_pad / 256)
+  int n_chunks;         // K_pad / 128
   int stages_per_cta;
-  int ksplit;
-  int group_size;
+  int ksplit;           // CTAs per cluster along K
+  int rows_per_group;   // group_size / 128
   int bias_dtype;
-  int S;               // ring depth
+  int S;                // ring depth
 };
 
 template <typename T> struct Ops;
@@ -66,29 +86,30 @@ template <> struct Ops<__half> {
   static constexpr uint32_t kMagicHi = 0x54005400u;  // 64 + nibble (bits 4..7)
   static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, kMagicLo); }
   static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t, 0x00F000F0u, kMagicHi); }
-  static __device__ __forceinline__ float off_lo() { return 1024.0f; }
-  static __device__ __forceinline__ float off_hi() { return 64.0f; }
-  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+  static constexpr uint32_t kOffLo2 = 0x64006400u, kOffHi2 = 0x54005400u;  // (1024, 1024), (64, 64)
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
     uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
+  // a (op) broadcast(lane of pair), round-to-nearest-even
+  static __device__ __forceinline__ uint32_t sub_l(uint32_t a, uint32_t pair, int lane) {
+    __half2 x = *reinterpret_cast<__half2*>(&a), p = *reinterpret_cast<__half2*>(&pair);
+    __half2 r = __hsub2(x, lane ? __high2half2(p) : __low2half2(p));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
-  static __device__ __forceinline__ uint32_t bcast(float v) {
-    __half h = __float2half_rn(v);
-    uint16_t u = *reinterpret_cast<uint16_t*>(&h);
-    return (uint32_t)u | ((uint32_t)u << 16);
+  // a (op) broadcast(lane of pair), round-to-nearest-even
+  static __device__ __forceinline__ uint32_t mul_l(uint32_t a, uint32_t pair, int lane) {
+    __half2 x = *reinterpret_cast<__half2*>(&a), p = *reinterpret_cast<__half2*>(&pair);
+    __half2 r = __hmul2(x, lane ? __high2half2(p) : __low2half2(p));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
   static __device__ __forceinline__ uint32_t pack2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
   static __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -100,29 +121,30 @@ template <> struct Ops<__nv_bfloat16> {
   static constexpr uint32_t kMagic = 0x43004300u;  // 128 + nibble (bits 0..3)
   static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, kMagic); }
   static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t >> 4, 0x000F000Fu, kMagic); }
-  static __device__ __forceinline__ float off_lo() { return 128.0f; }
-  static __device__ __forceinline__ float off_hi() { return 128.0f; }
-  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+  static constexpr uint32_t kOffLo2 = 0x43004300u, kOffHi2 = 0x43004300u;  // (128, 128)
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
     uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
+  // a (op) broadcast(lane of pair), round-to-nearest-even
+  static __device__ __forceinline__ uint32_t sub_l(uint32_t a, uint32_t pair, int lane) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a), p = *reinterpret_cast<__nv_bfloat162*>(&pair);
+    __nv_bfloat162 r = __hsub2(x, lane ? __high2bfloat162(p) : __low2bfloat162(p));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
-  static __device__ __forceinline__ uint32_t bcast(float v) {
-    __nv_bfloat16 h = __float2bfloat16_rn(v);
-    uint16_t u = *reinterpret_cast<uint16_t*>(&h);
-    return (uint32_t)u | ((uint32_t)u << 16);
+  // a (op) broadcast(lane of pair), round-to-nearest-even
+  static __device__ __forceinline__ uint32_t mul_l(uint32_t a, uint32_t pair, int lane) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a), p = *reinterpret_cast<__nv_bfloat162*>(&pair);
+    __nv_bfloat162 r = __hmul2(x, lane ? __high2bfloat162(p) : __low2bfloat162(p));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
   static __device__ __forceinline__ uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
   static __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -135,100 +157,80 @@ __device__ __forceinline__ constexpr uint32_t pair_sel(int bp) {
   return (uint32_t)bp | ((uint32_t)bp << 4) | ((uint32_t)(4 + bp) << 8) | ((uint32_t)(4 + bp) << 12);
 }
 
-// CTAs per SM the launch bounds (and the shared-memory ring depth) are sized for.
-constexpr int ctas_per_sm(int wn, int nt) { return nt == 4 ? 1 : (wn == 4 ? 2 : (wn == 2 ? 3 : 6)); }
+// round(round(v) + bias) for 4 consecutive columns, stored to out[m, col..col+3]
+template <typename XT>
+__device__ __forceinline__ void finalize4(const Args& a, int m, int col, float4 v) {
+  float r[4] = {v.x, v.y, v.z, v.w};
+  __align__(8) XT o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float t = round_to<XT>(r[j]);
+    if (a.bias) t += load_as_f32(a.bias, col + j, a.bias_dtype);
+    o[j] = Num<XT>::from_f(t);
+  }
+  XT* dst = static_cast<XT*>(a.out) + (int64_t)m * a.ldo + col;
+  if (aligned(dst, 8)) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = o[j];
+  }
+}
 
-template <typename XT, typename PT, int WN, int NT>
-__global__ void __launch_bounds__(32 * (WN + 1), ctas_per_sm(WN, NT)) gemv_int4_kernel(const __grid_constant__ CUtensorMap wmap,
-                                                                  const __grid_constant__ CUtensorMap xmap,
-                                                                  const Args args) {
+__device__ __forceinline__ void add4(float4& v, const float4& f) {
+  v.x += f.x;
+  v.y += f.y;
+  v.z += f.z;
+  v.w += f.w;
+}
+
+template <typename XT, typename PT, int NT>
+__global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
+    gemv_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                     const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
+                     const Args args) {
+  constexpr int WK = warps_k(NT);
+  static_assert(WK == 2 * kPairs, "consumer warps come in pairs");
   constexpr bool kExact = std::is_same<XT, PT>::value;  // dequant in half2 with exact rounding
   constexpr int kMPad = 8 * NT;
-  constexpr int kStage = stage_bytes(WN, NT);
-  constexpr int kXOff = WN * kWBoxBytes;
-  constexpr int kSOff = kXOff + x_bytes(NT);
-  constexpr int kZOff = kSOff + WN * kWarpCols * 2;
+  constexpr int kXChunk = x_chunk_bytes(NT);
+  constexpr int kStage = stage_bytes(NT);
+  constexpr int kConsumers = WK * 32;
   using O = Ops<XT>;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
   const int S = args.S;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStage);
+  int ring = S * kStage;
+  if (ring < red_bytes(NT)) ring = red_bytes(NT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
-  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int cb = blockIdx.x;
+  const int n0 = blockIdx.x * kCols;
   const int sp = blockIdx.y;
-  const int n0 = cb * WN * kWarpCols;
   const int st_begin = sp * args.stages_per_cta;
   int st_end = st_begin + args.stages_per_cta;
   if (st_end > args.n_stages) st_end = args.n_stages;
   const int n_it = st_end > st_begin ? st_end - st_begin : 0;
+  int valid_cols = args.N - n0;
+  if (valid_cols > kCols) valid_cols = kCols;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], WN);
+      mbar_init(&empty[i], 2);  // the two warps of a pair
     }
     *abort_flag = 0;
-    *last_flag = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
 
-  if (warp == WN) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tensormap(&wmap);
-      prefetch_tensormap(&xmap);
-      const uint64_t pol = l2_policy_evict_first();
-      int valid_cols = args.N - n0;
-      if (valid_cols > WN * kWarpCols) valid_cols = WN * kWarpCols;
-      const int wn_valid = (valid_cols + kWarpCols - 1) / kWarpCols;
-      const uint32_t bytes = (uint32_t)(wn_valid * kWBoxBytes + x_bytes(NT) + 2 * valid_cols * 2);
-      const char* sbase = static_cast<const char*>(args.scales);
-      const char* zbase = static_cast<const char*>(args.zeros);
-      int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int slot = it % S;
-        const uint32_t ph = (uint32_t)(it / S) & 1u;
-        if (it >= S) {
-          if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, args.err, 1)) {
-            *abort_flag = 1;
-            break;
-          }
-        }
-        if (*abort_flag) break;
-        uint8_t* st = smem + slot * kStage;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        const int stage = st_begin + it;
-        for (int w = 0; w < wn_valid; ++w)
-          tma_load_2d_hint(st + w * kWBoxBytes, &wmap, &full[slot], n0 + w * kWarpCols, stage * kRowsPerStage,
-                           pol);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) tma_load_2d(st + kXOff + s * kMPad * 32, &xmap, &full[slot], stage * 128 + 16 * s, 0);
-        const int64_t grow = ((int64_t)stage * 128) / args.group_size;
-        bulk_load(st + kSOff, sbase + (grow * args.N + n0) * 2, (uint32_t)valid_cols * 2, &full[slot]);
-        bulk_load(st + kZOff, zbase + (grow * args.N + n0) * 2, (uint32_t)valid_cols * 2, &full[slot]);
-        issued = it + 1;
-      }
-      if (*abort_flag) {
-        // drain: wait (bounded) for the copies this CTA still has in flight
-        for (int it = (issued > S ? issued - S : 0); it < issued; ++it)
-          mbar_wait_bounded(&full[it % S], (uint32_t)(it / S) & 1u, args.err, 4);
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
   const int g = lane >> 2;  // MMA group id: A row / B column
   const int q = lane & 3;   // thread in group
-  const bool warp_active = (n0 + warp * kWarpCols) < args.N;
   float acc[NT][8][4];
 #pragma unroll
   for (int a = 0; a < NT; ++a)
@@ -237,245 +239,224 @@ __global__ void __launch_bounds__(32 * (WN + 1), ctas_per_sm(WN, NT)) gemv_int4_
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[a][t][e] = 0.0f;
 
-  for (int it = 0; it < n_it; ++it) {
-    const int slot = it % S;
-    const uint32_t ph = (uint32_t)(it / S) & 1u;
-    if (!mbar_wait_bounded(&full[slot], ph, args.err, 2)) {
-      *abort_flag = 1;
-      break;
+  if (warp == WK) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&xmap);
+      prefetch_tensormap(&smap);
+      prefetch_tensormap(&zmap);
+      const uint64_t pol = l2_policy_evict_first();
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int slot = it % S;
+        if (it >= S) {
+          if (!mbar_wait_bounded(&empty[slot], (uint32_t)(it / S - 1) & 1u, args.err, 1)) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+        if (*abort_flag) break;
+        uint8_t* st = smem + slot * kStage;
+        const int stage = st_begin + it;
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)stage_tx_bytes(NT));
+        tma_load_2d_hint(st, &wmap, &full[slot], n0, stage * kWRows, pol);
+        tma_load_3d(st + x_off(), &xmap, &full[slot], 0, 0, stage * (kStageK / 16));
+        const int srow = (2 * stage) / args.rows_per_group;
+        tma_load_2d(st + s_off(NT), &smap, &full[slot], n0, srow);
+        tma_load_2d(st + z_off(NT), &zmap, &full[slot], n0, srow);
+        issued = it + 1;
+      }
+      if (*abort_flag) {
+        // drain: wait (bounded) for the copies this CTA still has in flight
+        for (int it = (issued > S ? issued - S : 0); it < issued; ++it)
+          mbar_wait_bounded(&full[it % S], (uint32_t)(it / S) & 1u, args.err, 4);
+      }
     }
-    const uint8_t* st = smem + slot * kStage;
-    if (warp_active) {
-      const uint8_t* wb = st + warp * kWBoxBytes;
-      const PT* sv = reinterpret_cast<const PT*>(st + kSOff) + warp * kWarpCols + 16 * g;
-      const PT* zv = reinterpret_cast<const PT*>(st + kZOff) + warp * kWarpCols + 16 * g;
-      // per-column dequant constants for this thread's 16 columns
-      uint32_t sc[16], zlo[16], zhi[16];
-      float sf[16], zf[16];
-      {
-        uint4 s4[2], z4[2];
-        s4[0] = reinterpret_cast<const uint4*>(sv)[0];
-        s4[1] = reinterpret_cast<const uint4*>(sv)[1];
-        z4[0] = reinterpret_cast<const uint4*>(zv)[0];
-        z4[1] = reinterpret_cast<const uint4*>(zv)[1];
-        const PT* sp_ = reinterpret_cast<const PT*>(s4);
-        const PT* zp_ = reinterpret_cast<const PT*>(z4);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float s = Num<PT>::to_f(sp_[i]);
-          const float z = Num<PT>::to_f(zp_[i]);
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int pair = warp >> 1;
+    const int h = warp & 1;  // which group of the stage
+    for (int it = pair; it < n_it; it += kPairs) {
+      const int slot = it % S;
+      if (*abort_flag) break;
+      if (!mbar_wait_bounded(&full[slot], (uint32_t)(it / S) & 1u, args.err, 2)) {
+        *abort_flag = 1;
+        break;
+      }
+      const int stage = st_begin + it;
+      const int chunk = 2 * stage + h;  // 128-k group-sized chunk index
+      if (chunk < args.n_chunks) {
+        const uint8_t* st = smem + slot * kStage;
+        const int srow = chunk / args.rows_per_group - (2 * stage) / args.rows_per_group;
+        const PT* sv = reinterpret_cast<const PT*>(st + s_off(NT)) + srow * kCols + 16 * g;
+        const PT* zv = reinterpret_cast<const PT*>(st + z_off(NT)) + srow * kCols + 16 * g;
+        // per-column dequant constants for this thread's 16 columns, kept as
+        // pairs (columns 2j, 2j+1); the lane is selected where they are used
+        uint32_t sc2[8], zlo2[8], zhi2[8];
+        float sf[16], zf[16];
+        {
+          uint4 s4[2], z4[2];
+          s4[0] = reinterpret_cast<const uint4*>(sv)[0];
+          s4[1] = reinterpret_cast<const uint4*>(sv)[1];
+          z4[0] = reinterpret_cast<const uint4*>(zv)[0];
+          z4[1] = reinterpret_cast<const uint4*>(zv)[1];
           if constexpr (kExact) {
-            sc[i] = O::bcast(s);
-            zlo[i] = O::bcast(O::off_lo() + z);  // exact: z is an integer in [0, 15]
-            zhi[i] = O::bcast(O::off_hi() + z);
+            const uint32_t* sw = reinterpret_cast<const uint32_t*>(s4);
+            const uint32_t* zw = reinterpret_cast<const uint32_t*>(z4);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              sc2[j] = sw[j];
+              zlo2[j] = O::add(zw[j], O::kOffLo2);  // exact: zeros are integers in [0, 15]
+              zhi2[j] = O::add(zw[j], O::kOffHi2);
+            }
           } else {
-            sf[i] = s;
-            zf[i] = z;
-          }
-        }
-      }
-#pragma unroll 2
-      for (int s = 0; s < 8; ++s) {
-        const int r0 = 8 * s + 2 * q;
-        const int r1 = r0 + 1;
-        const uint4 wa = *reinterpret_cast<const uint4*>(wb + r0 * 128 + ((g ^ (r0 & 7)) << 4));
-        const uint4 wbv = *reinterpret_cast<const uint4*>(wb + r1 * 128 + ((g ^ (r1 & 7)) << 4));
-        uint32_t b0[NT], b1[NT];
+            const PT* sp_ = reinterpret_cast<const PT*>(s4);
+            const PT* zp_ = reinterpret_cast<const PT*>(z4);
 #pragma unroll
-        for (int a = 0; a < NT; ++a) {
-          const uint2 xv =
-              *reinterpret_cast<const uint2*>(st + kXOff + s * kMPad * 32 + (a * 8 + g) * 32 + q * 8);
-          b0[a] = __byte_perm(xv.x, xv.y, 0x5410);  // (x[4q], x[4q+2])
-          b1[a] = __byte_perm(xv.x, xv.y, 0x7632);  // (x[4q+1], x[4q+3])
-        }
-        const uint32_t wa_w[4] = {wa.x, wa.y, wa.z, wa.w};
-        const uint32_t wb_w[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          uint32_t afr[4];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int i = 2 * t + h;
-            const uint32_t tt = __byte_perm(wa_w[i >> 2], wb_w[i >> 2], pair_sel(i & 3));
-            if constexpr (kExact) {
-              afr[h] = O::mul(O::sub(O::lo(tt), zlo[i]), sc[i]);
-              afr[2 + h] = O::mul(O::sub(O::hi(tt), zhi[i]), sc[i]);
-            } else {
-              const float a_lo = (float)(tt & 15u), a_hi = (float)((tt >> 4) & 15u);
-              const float b_lo = (float)((tt >> 16) & 15u), b_hi = (float)((tt >> 20) & 15u);
-              afr[h] = O::pack2((a_lo - zf[i]) * sf[i], (b_lo - zf[i]) * sf[i]);
-              afr[2 + h] = O::pack2((a_hi - zf[i]) * sf[i], (b_hi - zf[i]) * sf[i]);
-            }
-          }
-#pragma unroll
-          for (int a = 0; a < NT; ++a) O::mma(acc[a][t], afr, b0[a], b1[a]);
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-  }
-
-  // ------------------------------------------------------------- epilogue
-  // Thread (g, q) holds, for token tile a, tokens a*8 + 2q (+1) and the 16
-  // consecutive columns n0 + 128*warp + 16g + c (c = 2t + h).
-  const int col0 = n0 + warp * kWarpCols + 16 * g;
-  const bool chunk_valid = warp_active && col0 < args.N;  // N % 8 == 0: a chunk is all valid or 8 valid
-  int chunk_cols = args.N - col0;
-  if (chunk_cols > 16) chunk_cols = 16;
-
-  auto finalize_store = [&](int m, const float* v) {
-    __align__(16) XT vals[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      float r = round_to<XT>(v[c]);
-      if (args.bias && c < chunk_cols) r += load_as_f32(args.bias, col0 + c, args.bias_dtype);
-      vals[c] = Num<XT>::from_f(r);
-    }
-    XT* dst = static_cast<XT*>(args.out) + (int64_t)m * args.ldo + col0;
-    if (chunk_cols == 16 && aligned(dst, 16)) {
-      reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(vals)[0];
-      reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(vals)[1];
-    } else {
-      for (int c = 0; c < chunk_cols; ++c) dst[c] = vals[c];
-    }
-  };
-
-  if (args.ksplit == 1) {
-    if (chunk_valid) {
-#pragma unroll
-      for (int a = 0; a < NT; ++a) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int m = a * 8 + 2 * q + e;
-          if (m < args.M) {
-            float v[16];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              v[2 * t] = acc[a][t][e];
-              v[2 * t + 1] = acc[a][t][2 + e];
-            }
-            finalize_store(m, v);
-          }
-        }
-      }
-    }
-    return;
-  }
-
-  // split-K: publish this CTA's partial sums
-  if (chunk_valid) {
-#pragma unroll
-    for (int a = 0; a < NT; ++a) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = a * 8 + 2 * q + e;
-        if (m < args.M) {
-          float* dst = args.partials + ((int64_t)sp * args.M + m) * args.N + col0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (4 * j < chunk_cols) {
-              float4 f;
-              f.x = acc[a][2 * j][e];
-              f.y = acc[a][2 * j][2 + e];
-              f.z = acc[a][2 * j + 1][e];
-              f.w = acc[a][2 * j + 1][2 + e];
-              __stcg(reinterpret_cast<float4*>(dst) + j, f);
+            for (int i = 0; i < 16; ++i) {
+              sf[i] = Num<PT>::to_f(sp_[i]);
+              zf[i] = Num<PT>::to_f(zp_[i]);
             }
           }
         }
-      }
-    }
-  }
-  __threadfence();
-  named_barrier(1, WN * 32);
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&args.tickets[cb], 1);
-    *last_flag = (prev == args.ksplit - 1) ? 1 : 0;
-  }
-  named_barrier(1, WN * 32);
-  if (!*last_flag) return;
-  __threadfence();
-  if (chunk_valid) {
+        const uint8_t* wbase = st + 64 * h * 128;                 // this group's 64 packed rows
+        const uint8_t* xbase = st + x_off() + 8 * h * kXChunk;    // this group's 8 x chunks
 #pragma unroll
-    for (int a = 0; a < NT; ++a) {
+        for (int s = 0; s < 8; ++s) {
+          const int r0 = 64 * h + 8 * s + 2 * q;  // row within the 128-row box (swizzle uses r & 7)
+          const int r1 = r0 + 1;
+          const uint4 wa = *reinterpret_cast<const uint4*>(wbase + (8 * s + 2 * q) * 128 + ((g ^ (r0 & 7)) << 4));
+          const uint4 wbv = *reinterpret_cast<const uint4*>(wbase + (8 * s + 2 * q + 1) * 128 + ((g ^ (r1 & 7)) << 4));
+          uint32_t b0[NT], b1[NT];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = a * 8 + 2 * q + e;
-        if (m < args.M) {
-          float own[16], v[16];
+          for (int a = 0; a < NT; ++a) {
+            const uint2 xv = *reinterpret_cast<const uint2*>(xbase + s * kXChunk + (a * 8 + g) * 32 + q * 8);
+            b0[a] = __byte_perm(xv.x, xv.y, 0x5410);  // (x[4q], x[4q+2])
+            b1[a] = __byte_perm(xv.x, xv.y, 0x7632);  // (x[4q+1], x[4q+3])
+          }
+          const uint32_t wa_w[4] = {wa.x, wa.y, wa.z, wa.w};
+          const uint32_t wb_w[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            own[2 * t] = acc[a][t][e];
-            own[2 * t + 1] = acc[a][t][2 + e];
-          }
+            uint32_t afr[4];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) v[c] = 0.0f;
-          for (int s2 = 0; s2 < args.ksplit; ++s2) {
-            if (s2 == sp) {
-#pragma unroll
-              for (int c = 0; c < 16; ++c) v[c] += own[c];
-            } else {
-              const float4* src =
-                  reinterpret_cast<const float4*>(args.partials + ((int64_t)s2 * args.M + m) * args.N + col0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                if (4 * j < chunk_cols) {
-                  const float4 f = __ldcg(src + j);
-                  v[4 * j] += f.x;
-                  v[4 * j + 1] += f.y;
-                  v[4 * j + 2] += f.z;
-                  v[4 * j + 3] += f.w;
-                }
+            for (int hh = 0; hh < 2; ++hh) {
+              const int i = 2 * t + hh;
+              const uint32_t tt = __byte_perm(wa_w[i >> 2], wb_w[i >> 2], pair_sel(i & 3));
+              if constexpr (kExact) {
+                afr[hh] = O::mul_l(O::sub_l(O::lo(tt), zlo2[i >> 1], hh), sc2[i >> 1], hh);
+                afr[2 + hh] = O::mul_l(O::sub_l(O::hi(tt), zhi2[i >> 1], hh), sc2[i >> 1], hh);
+              } else {
+                const float a_lo = (float)(tt & 15u), a_hi = (float)((tt >> 4) & 15u);
+                const float b_lo = (float)((tt >> 16) & 15u), b_hi = (float)((tt >> 20) & 15u);
+                afr[hh] = O::pack2((a_lo - zf[i]) * sf[i], (b_lo - zf[i]) * sf[i]);
+                afr[2 + hh] = O::pack2((a_hi - zf[i]) * sf[i], (b_hi - zf[i]) * sf[i]);
               }
             }
+#pragma unroll
+            for (int a = 0; a < NT; ++a) O::mma(acc[a][t], afr, b0[a], b1[a]);
           }
-          finalize_store(m, v);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+  }
+
+  // ---------------------------------------------------------- reduction
+  // The ring is free once every stage is consumed: reuse it as
+  // red[WK][M_pad][kRedPitch] (per warp) and cta[M_pad][kRedPitch].
+  float* red = reinterpret_cast<float*>(smem);
+  float* cta = red + (size_t)WK * kMPad * kRedPitch;
+  const int rows = args.M < kMPad ? args.M : kMPad;
+  const int tid = threadIdx.x;
+  if (warp < WK) {
+    named_barrier(1, kConsumers);
+#pragma unroll
+    for (int a = 0; a < NT; ++a) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = a * 8 + 2 * q + e;
+        if (m < rows) {
+          float4* dst = reinterpret_cast<float4*>(red + ((size_t)warp * kMPad + m) * kRedPitch + 16 * g);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_float4(acc[a][2 * j][e], acc[a][2 * j][2 + e], acc[a][2 * j + 1][e], acc[a][2 * j + 1][2 + e]);
         }
       }
     }
+    named_barrier(1, kConsumers);
+    for (int idx = tid; idx < rows * (kCols / 4); idx += kConsumers) {
+      const int m = idx / (kCols / 4), c4 = idx % (kCols / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < WK; ++w) add4(v, reinterpret_cast<const float4*>(red + ((size_t)w * kMPad + m) * kRedPitch)[c4]);
+      if (args.ksplit == 1) {
+        if (4 * c4 < valid_cols) finalize4<XT>(args, m, n0 + 4 * c4, v);
+      } else {
+        reinterpret_cast<float4*>(cta + (size_t)m * kRedPitch)[c4] = v;
+      }
+    }
   }
-  if (threadIdx.x == 0) args.tickets[cb] = 0;
+  if (args.ksplit == 1) return;
+
+  // split-K across the cluster: rank r finalises columns [32r/ks, 32(r+1)/ks) (in float4s)
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  if (warp < WK) {
+    const int ks = args.ksplit;
+    const int r = (int)cluster.block_rank();
+    const int c_lo = (kCols / 4) * r / ks, c_hi = (kCols / 4) * (r + 1) / ks;
+    const int width = c_hi - c_lo;
+    for (int idx = tid; idx < rows * width; idx += kConsumers) {
+      const int m = idx / width, c4 = c_lo + idx % width;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < ks; ++j) {
+        const float* peer = cluster.map_shared_rank(cta, j);
+        add4(v, reinterpret_cast<const float4*>(peer + (size_t)m * kRedPitch)[c4]);
+      }
+      if (4 * c4 < valid_cols) finalize4<XT>(args, m, n0 + 4 * c4, v);
+    }
+  }
+  cluster.sync();  // peers may still read this CTA's tile
 }
 
 // ---------------------------------------------------------------- host side
 struct Plan {
-  int wn, nt, S, ksplit, spc, n_cb;
+  int nt, S, ksplit, spc, n_cb, n_stages;
   size_t smem;
 };
 
 static Plan make_plan(int64_t M, int64_t N, int64_t K_pad) {
   Plan p{};
   p.nt = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
-  const int64_t n_stages = K_pad / 128;
+  p.n_stages = (int)cdiv(K_pad, kStageK);
   const int sms = num_sms();
-  // Prefer wide CTAs (x slice shared by more warps); fall back to narrower ones
-  // when there are too few (column block, stage) units to fill the GPU.
-  int wn = 4;
-  if (p.nt < 4) {  // the M <= 32 variant keeps 4 warps (its accumulators need the register budget)
-    for (int cand : {4, 2, 1}) {
-      wn = cand;
-      const int64_t n_cb = cdiv(N, (int64_t)cand * kWarpCols);
-      if (n_cb * n_stages >= 2LL * sms) break;
-    }
-  }
-  p.wn = wn;
-  p.n_cb = (int)cdiv(N, (int64_t)wn * kWarpCols);
-  const int per_sm = ctas_per_sm(wn, p.nt);
+  const int per_sm = ctas_per_sm(p.nt);
+  p.n_cb = (int)cdiv(N, kCols);
   const size_t budget = (size_t)(227 * 1024) / per_sm - 2048;
-  const size_t stage = (size_t)stage_bytes(wn, p.nt);
+  const size_t stage = (size_t)stage_bytes(p.nt);
+  // Ring slot i always holds stages i, i+S, ... of the same warp pair only if S
+  // is a multiple of the pair count: then a pair waits on the phases of its
+  // slots in order and an mbarrier parity wait can never alias a phase that
+  // belongs to the other pair.
   int S = (int)(budget / stage);
-  if (S > 4) S = 4;
-  if (S < 2) S = 2;
+  if (S > 8) S = 8;
+  S = (S / kPairs) * kPairs;
+  if (S < kPairs) S = kPairs;
   p.S = S;
-  p.smem = (size_t)S * stage + 1024 + 2 * S * 8 + 64;
+  size_t ring = (size_t)S * stage;
+  if (ring < (size_t)red_bytes(p.nt)) ring = red_bytes(p.nt);
+  p.smem = ring + 1024 + 2 * S * 8 + 64;
   const int64_t target = (int64_t)per_sm * sms;
-  int64_t ks = cdiv(target, p.n_cb);
-  if (ks > n_stages) ks = n_stages;
+  int64_t ks = (target + p.n_cb / 2) / p.n_cb;
+  if (ks > p.n_stages) ks = p.n_stages;
+  if (ks > kMaxCluster) ks = kMaxCluster;
   if (ks < 1) ks = 1;
-  const int64_t spc = cdiv(n_stages, ks);
+  const int64_t spc = cdiv(p.n_stages, ks);
   p.spc = (int)spc;
-  p.ksplit = (int)cdiv(n_stages, spc);
+  p.ksplit = (int)cdiv(p.n_stages, spc);
   return p;
 }
 
@@ -486,25 +467,18 @@ bool gemv_supported(const QLinearProblem& pb) {
   if (!(pb.x_dtype == TF_F16 || pb.x_dtype == TF_BF16)) return false;
   if (!(pb.param_dtype == TF_F16 || pb.param_dtype == TF_BF16)) return false;
   if (pb.group_size % 128 != 0 || pb.K_pad % 128 != 0 || pb.K_pad == 0) return false;
-  if (pb.N % 16 != 0 || pb.ldx % 8 != 0 || pb.K % 8 != 0) return false;
+  if (pb.N % 16 != 0 || pb.ldx % 8 != 0 || pb.K % 16 != 0 || pb.K == 0) return false;
   if (!aligned(pb.x, 16) || !aligned(pb.packed, 16) || !aligned(pb.scales, 16) || !aligned(pb.zeros, 16))
     return false;
   if (pb.N > 0x7fffffffLL || pb.K_pad / 2 > 0x7fffffffLL) return false;
   return true;
 }
 
-size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K_pad) {
-  if (M < 1 || M > 32 || K_pad < 128 || N < 1) return kWsHeader;
-  gemv::Plan p = gemv::make_plan(M, N, K_pad);
-  size_t b = kWsHeader + (size_t)cdiv((int64_t)p.n_cb * 4, 256) * 256;
-  if (p.ksplit > 1) b += (size_t)p.ksplit * M * N * 4;
-  return b;
-}
+size_t gemv_workspace_bytes(int64_t, int64_t, int64_t) { return kWsHeader; }
 
-template <typename XT, typename PT, int WN, int NT>
-static int launch_t(const QLinearProblem& pb, const gemv::Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap,
-                    gemv::Args a, cudaStream_t st) {
-  auto kern = gemv::gemv_int4_kernel<XT, PT, WN, NT>;
+template <typename XT, typename PT, int NT>
+static int launch_t(const gemv::Plan& p, const CUtensorMap* maps, const gemv::Args& a, cudaStream_t st) {
+  auto kern = gemv::gemv_int4_kernel<XT, PT, NT>;
   static bool attr_set[64] = {false};  // per template instance and device
   const int dev = current_device() & 63;
   if (!attr_set[dev]) {
@@ -512,62 +486,78 @@ static int launch_t(const QLinearProblem& pb, const gemv::Plan& p, const CUtenso
       return check_launch("gemv set smem attribute");
     attr_set[dev] = true;
   }
-  dim3 grid((unsigned)p.n_cb, (unsigned)p.ksplit);
-  kern<<<grid, 32 * (WN + 1), p.smem, st>>>(wmap, xmap, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.n_cb, (unsigned)p.ksplit, 1);
+  cfg.blockDim = dim3(32 * (gemv::warps_k(NT) + 1), 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)p.ksplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.ksplit > 1 ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], a);
+  if (e != cudaSuccess) return fail(TF_ERR_CUDA, "gemv_int4 launch: %s", cudaGetErrorString(e));
   return check_launch("gemv_int4");
 }
 
 template <typename XT, typename PT>
-static int launch_wn(const QLinearProblem& pb, const gemv::Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap,
-                     const gemv::Args& a, cudaStream_t st) {
-  if (p.nt == 4) return launch_t<XT, PT, 4, 4>(pb, p, wmap, xmap, a, st);  // plan forces WN = 4
-#define TF_GEMV_NT(WN)                                                              \
-  switch (p.nt) {                                                                   \
-    case 1: return launch_t<XT, PT, WN, 1>(pb, p, wmap, xmap, a, st);               \
-    default: return launch_t<XT, PT, WN, 2>(pb, p, wmap, xmap, a, st);              \
+static int launch_nt(const gemv::Plan& p, const CUtensorMap* maps, const gemv::Args& a, cudaStream_t st) {
+  switch (p.nt) {
+    case 1: return launch_t<XT, PT, 1>(p, maps, a, st);
+    case 2: return launch_t<XT, PT, 2>(p, maps, a, st);
+    default: return launch_t<XT, PT, 4>(p, maps, a, st);
   }
-  if (p.wn == 4) { TF_GEMV_NT(4) }
-  if (p.wn == 2) { TF_GEMV_NT(2) }
-  TF_GEMV_NT(1)
-#undef TF_GEMV_NT
 }
 
 int gemv_launch(const QLinearProblem& pb, cudaStream_t st) {
   gemv::Plan p = gemv::make_plan(pb.M, pb.N, pb.K_pad);
-  const size_t need = gemv_workspace_bytes(pb.M, pb.N, pb.K_pad);
-  if (!pb.workspace || pb.workspace_bytes < need)
-    return fail(TF_ERR_WORKSPACE, "qlinear(gemv): workspace %zu bytes < required %zu", pb.workspace_bytes, need);
-  CUtensorMap wmap, xmap;
-  int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, pb.packed, (uint64_t)pb.N,
-                                (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, gemv::kWarpCols, gemv::kRowsPerStage,
+  if (!pb.workspace || pb.workspace_bytes < kWsHeader)
+    return fail(TF_ERR_WORKSPACE, "qlinear(gemv): workspace %zu bytes < required %zu", pb.workspace_bytes,
+                (size_t)kWsHeader);
+  CUtensorMap maps[4];
+  // packed weights [K_pad/2 rows, N bytes], box 128 x 128 rows, 128-byte swizzle
+  int rc = encode_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, pb.packed, (uint64_t)pb.N,
+                                (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, gemv::kCols, gemv::kWRows,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, (uint64_t)pb.K, (uint64_t)pb.M,
-                            (uint64_t)pb.ldx * 2, 16, (uint32_t)(8 * p.nt), CU_TENSOR_MAP_SWIZZLE_NONE);
+  // x viewed as [K/16 chunks][M rows][16 k]: dims (16, M, K/16), strides (ldx*2, 32) bytes; box (16, M_pad, 16)
+  {
+    const uint64_t dims[3] = {16, (uint64_t)pb.M, (uint64_t)(pb.K / 16)};
+    const uint64_t strides[2] = {(uint64_t)pb.ldx * 2, 32};
+    const uint32_t box[3] = {16, (uint32_t)(8 * p.nt), 16};
+    rc = encode_tensor_map_3d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  const int64_t groups = pb.K_pad / pb.group_size;
+  rc = encode_tensor_map_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.scales, (uint64_t)pb.N, (uint64_t)groups,
+                            (uint64_t)pb.N * 2, gemv::kCols, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  char* ws = static_cast<char*>(pb.workspace);
+  rc = encode_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.zeros, (uint64_t)pb.N, (uint64_t)groups,
+                            (uint64_t)pb.N * 2, gemv::kCols, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
   gemv::Args a{};
-  a.scales = pb.scales;
-  a.zeros = pb.zeros;
   a.bias = pb.bias;
   a.bias_dtype = pb.bias_dtype;
   a.out = pb.out;
   a.ldo = pb.ldo;
-  a.err = reinterpret_cast<int*>(ws);
-  a.tickets = reinterpret_cast<int*>(ws + kWsHeader);
-  a.partials = reinterpret_cast<float*>(ws + kWsHeader + cdiv((int64_t)p.n_cb * 4, 256) * 256);
+  a.err = reinterpret_cast<int*>(pb.workspace);
   a.M = (int)pb.M;
   a.N = (int)pb.N;
-  a.n_stages = (int)(pb.K_pad / 128);
+  a.n_stages = p.n_stages;
+  a.n_chunks = (int)(pb.K_pad / 128);
   a.stages_per_cta = p.spc;
   a.ksplit = p.ksplit;
-  a.group_size = pb.group_size;
+  a.rows_per_group = pb.group_size / 128;
   a.S = p.S;
   const bool xh = pb.x_dtype == TF_F16, ph = pb.param_dtype == TF_F16;
-  if (xh && ph) return launch_wn<__half, __half>(pb, p, wmap, xmap, a, st);
-  if (!xh && !ph) return launch_wn<__nv_bfloat16, __nv_bfloat16>(pb, p, wmap, xmap, a, st);
-  if (xh && !ph) return launch_wn<__half, __nv_bfloat16>(pb, p, wmap, xmap, a, st);
-  return launch_wn<__nv_bfloat16, __half>(pb, p, wmap, xmap, a, st);
+  if (xh && ph) return launch_nt<__half, __half>(p, maps, a, st);
+  if (!xh && !ph) return launch_nt<__nv_bfloat16, __nv_bfloat16>(p, maps, a, st);
+  if (xh && !ph) return launch_nt<__half, __nv_bfloat16>(p, maps, a, st);
+  return launch_nt<__nv_bfloat16, __half>(p, maps, a, st);
 }
 
 }  // namespace tf
