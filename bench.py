@@ -1,0 +1,404 @@
+"""Decode benchmark: Qwen2.5-shaped int4 model on the B200 kernels.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--model 0.5b] [--batch 8] [--prompt 128]
+
+Workload (default): the Qwen2.5-0.5B architecture, random init (seed 0, fp16),
+every q/k/v/o/gate/up/down an int4 group-128 QuantLinear, batch 8, prompts of
+128 uniform-random token ids, greedy decode. One step = one decoded token for
+each of the B sequences (all layers, lm_head, argmax), run as one CUDA graph.
+
+Prints one JSON line. `value` is decode tokens/s over all ranks, timed on the
+device (CUDA events, max over ranks) with tokens fed back on the device; `e2e`
+is the same metric through the decoder's public step with the step's input
+tokens copied from pinned host memory and its output tokens read back every
+step. With N > 1 every rank decodes its own batch (independent replicas: the
+0.5B model is not sharded). `roofline` is the int4 GEMV (the kernel that
+streams the weights), its launches of one step timed live on its stream.
+`cpu_baseline` times the reference's CPU path (transformers Qwen2 with the
+reference's dequantize-then-matmul QuantLinear, restated in oracle/) on a
+bounded sample of decode steps on this host's cores.
+
+`--impl reference` times that same CPU path as the reference arm (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "int4 GEMV HBM GB/s (% of peak) at decode; Qwen2.5-shape decode tok/s at 1/2/4/8 GPU"
+
+
+def _peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        loaded = [v for v in sm if mx and v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        torch.cuda.set_device(local) if torch.cuda.is_available() else None
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_model(args, device):
+    """Random-init model (seeded) on the GPU, patched with int4 QuantLinears;
+    also returns an unpatched CPU copy for the CPU baseline when asked."""
+    import copy
+
+    import torch
+
+    from tritonforge_b200.decode import random_qwen2
+    from tritonforge_b200.integration import patch_model
+
+    model = random_qwen2(args.model, seed=0)
+    cpu_copy = copy.deepcopy(model) if args.want_cpu else None
+    model = model.to(device)
+    patch_model(model, group_size=128, dtype=torch.float16)
+    return model, cpu_copy
+
+
+def prompt_ids(args, vocab: int, rank: int):
+    import torch
+
+    g = torch.Generator().manual_seed(1000 + rank)
+    return torch.randint(0, vocab, (args.batch, args.prompt), generator=g)
+
+
+def cpu_decode_rate(cpu_model, prompt, steps: int, budget_s: float) -> tuple[float, int, int, str]:
+    """Decode tok/s of the reference's CPU path on this host (bounded sample)."""
+    import torch
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    with torch.no_grad():
+        out = cpu_model(prompt, use_cache=True)
+        past = out.past_key_values
+        nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
+        done, t0 = 0, time.perf_counter()
+        while done < steps:
+            out = cpu_model(nxt, past_key_values=past, use_cache=True)
+            past = out.past_key_values
+            nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+    b = prompt.shape[0]
+    sample = f"{done} decode steps x batch {b} after a {prompt.shape[1]}-token prefill, {dt:.1f} s"
+    return b * done / dt, cores, done, sample
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    import torch
+
+    from oracle.cpu_decode import cpu_reference_model
+    from tritonforge_b200.decode import random_qwen2
+
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    if dev is None:
+        print(json.dumps({"impl": "reference", "unavailable": "needs a CUDA device to build the int4 weights"}))
+        return
+    args.want_cpu = True
+    model, cpu_copy = build_model(args, dev)
+    cpu_model = cpu_reference_model(cpu_copy, model)
+    del model
+    torch.cuda.empty_cache()
+    prompt = prompt_ids(args, cpu_model.config.vocab_size, 0)
+    budget = float(os.environ.get("TF_REF_BUDGET_S", "120"))
+    rate, cores, done, sample = cpu_decode_rate(cpu_model, prompt, args.steps, budget)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": done, "warmup": 0, "ms_per_step": 1000.0 * args.batch / rate, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random-init weights, random token ids)",
+        "config": _config(args),
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def _config(args) -> dict:
+    return {"workload": f"Qwen2.5-{args.model.upper()}-shaped int4 g128 greedy decode", "model": f"qwen2.5-{args.model}",
+            "batch_per_gpu": args.batch, "prompt_len": args.prompt, "global_batch": args.batch * args.gpus,
+            "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+            "weights": "int4 group-128 K-major (fp16 scales/zeros); embeddings/norms/lm_head fp16",
+            "l2": "per-step working set (int4 weights + fp16 lm_head) exceeds the 126 MB L2"}
+
+
+def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
+    """Time the step's int4 GEMV launches alone (same shapes, weights and
+    inputs) in a CUDA graph; achieved = algorithmic bytes / measured time."""
+    import torch
+
+    from tritonforge_b200 import kernels
+
+    b = dec.buf
+    launches = []
+    for L in dec.layers:
+        launches += [(b["normed"], L["qkv"], b["qkv"]), (b["attn"], L["o"], b["o"]),
+                     (b["normed"], L["gu"], b["gu"]), (b["act"], L["down"], b["mlp"])]
+
+    def run():
+        for x, ql, out in launches:
+            kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
+
+    s = torch.cuda.Stream(dec.dev)
+    with torch.cuda.stream(s):
+        run()
+    torch.cuda.synchronize(dec.dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        run()
+    g.replay()
+    torch.cuda.synchronize(dec.dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize(dec.dev)
+    total_us = e0.elapsed_time(e1) * 1e3 / reps
+    alg = 0
+    for x, ql, out in launches:
+        m, k = x.shape
+        kp, n = ql.packed.shape[0] * 2, ql.packed.shape[1]
+        alg += m * k * 2 + kp * n // 2 + 2 * (kp // ql.group_size) * n * 2 + m * n * 2
+        if ql.bias is not None:
+            alg += n * 2
+    achieved = alg / (total_us * 1e-6) / 1e9
+    return {"kernel": "gemv_int4 (tf_qlinear decode regime)", "bound": "hbm", "achieved": achieved,
+            "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs, "traffic": None,
+            "launches_per_step": len(launches), "algorithmic_bytes_per_step": alg,
+            "us_per_launch": total_us / len(launches)}
+
+
+def run_ours(args) -> None:
+    world, rank, local = _dist()
+    import torch
+    import torch.distributed as dist
+
+    from tritonforge_b200.decode import QwenDecoder
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    args.want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
+    model, cpu_copy = build_model(args, dev)
+    vocab = model.config.vocab_size
+    prompt = prompt_ids(args, vocab, rank)
+    max_len = args.prompt + args.warmup + 2 * args.steps + 8
+    dec = QwenDecoder(model, batch=args.batch, max_len=max_len)
+    # prefill in chunks of M <= 32 rows so every projection runs the decode kernel
+    chunk = max(1, 32 // args.batch)
+    with torch.no_grad():
+        from transformers import DynamicCache
+
+        cache = DynamicCache()
+        for c0 in range(0, args.prompt, chunk):
+            out = model(prompt[:, c0:c0 + chunk].to(dev), past_key_values=cache, use_cache=True)
+            cache = out.past_key_values
+        from tritonforge_b200.decode import _layer_kv
+
+        for li in range(len(dec.layers)):
+            k, v = _layer_kv(cache, li)
+            dec.k_cache[li, :, :, :args.prompt].copy_(k)
+            dec.v_cache[li, :, :, :args.prompt].copy_(v)
+        dec.tokens.copy_(out.logits[:, -1, :].argmax(-1))
+        dec.pos.copy_(torch.tensor([args.prompt, args.prompt + 1], dtype=torch.int32))
+        del cache, out
+    dec.capture()
+    for _ in range(args.warmup):
+        dec.replay()
+    torch.cuda.synchronize(dev)
+    launches_per_step = 9 * len(dec.layers) + 1
+
+    # ---- device-timed decode (tokens fed back on the device)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            dec.graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    value = world * args.batch * args.steps / (ms / 1000.0)
+
+    # ---- end to end: per step H2D of the input tokens (pinned) + D2H of the output tokens
+    host_in = torch.empty(args.batch, dtype=torch.long, pin_memory=True)
+    host_out = torch.empty(args.batch, dtype=torch.long, pin_memory=True)
+    host_in.copy_(dec.tokens.cpu())
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    s = torch.cuda.current_stream(dev)
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(s)
+    for _ in range(args.steps):
+        dec.tokens.copy_(host_in, non_blocking=True)
+        dec.graph.replay()
+        host_out.copy_(dec.tokens, non_blocking=True)
+        s.synchronize()
+        host_in.copy_(host_out)
+    f1.record(s)
+    torch.cuda.synchronize(dev)
+    e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
+    e2e_value = world * args.batch * args.steps / (e2e_ms / 1000.0)
+
+    peaks = _peaks()
+    roof = gemv_roofline(dec, peaks["hbm_gbs"])
+    roof["peak_source"] = peaks["source"]
+
+    cpu = None
+    if rank == 0 and args.want_cpu:
+        from oracle.cpu_decode import cpu_reference_model
+
+        cpu_model = cpu_reference_model(cpu_copy, model)
+        rate, cores, _, sample = cpu_decode_rate(cpu_model, prompt, 1000, float(args.cpu_budget))
+        cpu = {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random-init weights, random token ids)",
+            "config": _config(args), "clocks": clocks.summary(),
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": host_in.numel() * 8,
+                    "d2h_bytes_per_step": host_out.numel() * 8},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del dec
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="0.5b", choices=["0.5b"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -136,6 +136,35 @@ int tf_dequantize_int4(const uint8_t* packed, const void* scales, const void* ze
 int tf_unpack_int4(const uint8_t* packed, uint8_t* codes, int64_t K_pad, int64_t N,
                    void* stream);
 
+/* ---- decode-loop support (Qwen2-shaped engine) ---------------------------
+ * No reference counterpart as kernels: the reference runs these steps through
+ * transformers' Qwen2 code (rotary embedding, SDPA attention, DynamicCache;
+ * reference src/tritonforge/integration/qwen.py:124-152 calls into them).
+ * They exist so a whole decode step, with positions and lengths read from
+ * device memory, can be captured in one CUDA graph.
+ *
+ * tf_rope_kv_append: qkv rows [B, (hq + 2*hkv) * D] (row stride ld_qkv
+ * elements) -> q_out [B, hq, D] rotated; k rotated and v appended to the
+ * caches [B, hkv, t_max, D] at position *pos (device int). cos/sin tables are
+ * [t_max, D] in the model dtype; rounding as transformers' apply_rotary_pos_emb.
+ */
+int tf_rope_kv_append(const void* qkv, int64_t ld_qkv, void* q_out, const void* cos_table,
+                      const void* sin_table, void* k_cache, void* v_cache, const int* pos,
+                      int64_t B, int32_t hq, int32_t hkv, int32_t head_dim, int64_t t_max, int dtype,
+                      void* stream);
+
+/* tf_decode_attention: out [B, hq, D] = softmax(q k^T * scale) v over the
+ * first *len (device int) cached positions; grouped-query (hq % hkv == 0),
+ * D in {64, 128}; fp32 scores/softmax/accumulation, one rounding. */
+int tf_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                        const int* len, int64_t B, int32_t hq, int32_t hkv, int32_t head_dim,
+                        int64_t t_max, float scale, int dtype, void* stream);
+
+/* tf_swiglu_strided: SwiGLU over row-strided gate/up views (e.g. the two
+ * halves of a fused gate|up projection), same math as tf_swiglu. */
+int tf_swiglu_strided(const void* gate, const void* up, void* out, int64_t M, int64_t N, int64_t ldg,
+                      int64_t ldu, int64_t ldo, int dtype, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

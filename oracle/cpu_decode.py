@@ -1,0 +1,76 @@
+"""CPU restatement of the reference's int4 Qwen2 decode path (TEST ORACLE ONLY;
+used by the tests and by bench.py's cpu_baseline / --impl reference legs).
+
+The reference's CPU-capable end-to-end path is transformers' Qwen2 model with
+its int4 QuantLinear on the dequantize-then-matmul branch
+(reference src/tritonforge/integration/qwen.py:91-97: dequantize the whole
+weight to the activation dtype every call, `x @ W[:K]`, `+ bias`), norms as
+transformers' RMSNorm and the MLP activation as `reference.swiglu_reference`
+(reference.py:53-57). `cpu_reference_model` restates that on CPU tensors:
+every projection's forward becomes `OracleQuantLinear.forward`, which runs the
+oracle's dequantizer (oracle.quant, bit-exact with quant.py) and a torch CPU
+matmul in the model dtype.
+"""
+
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import quant as oquant
+
+_NP = {torch.float16: "float16", torch.bfloat16: "bfloat16"}
+
+
+class OracleQuantLinear(nn.Module):
+    """int4 linear computed the reference's dequantize-then-matmul way on CPU."""
+
+    def __init__(self, packed: np.ndarray, scales: torch.Tensor, zeros: torch.Tensor, in_features: int,
+                 out_features: int, bias: torch.Tensor | None, group_size: int) -> None:
+        super().__init__()
+        self.packed = packed
+        self.scales = scales.float().numpy()
+        self.zeros = zeros.float().numpy()
+        self.bias = bias
+        self.in_features = in_features
+        self.out_features = out_features
+        self.group_size = group_size
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dense = oquant.dequantize_int4_f32(self.packed, self.scales, self.zeros, self.group_size)
+        w = torch.from_numpy(dense[: self.in_features]).to(x.dtype)     # quant.py:105 (cast)
+        shape = x.shape
+        out = x.reshape(-1, shape[-1]) @ w                                # qwen.py:95
+        if self.bias is not None:
+            out = out + self.bias                                         # qwen.py:96-97
+        return out.reshape(*shape[:-1], self.out_features)
+
+
+def _swiglu_mlp_forward(self, x):
+    g = self.gate_proj(x).float()
+    u = self.up_proj(x).float()
+    act = ((g * torch.sigmoid(g)) * u).to(x.dtype)                       # reference.py:53-57
+    return self.down_proj(act)
+
+
+def cpu_reference_model(cpu_model, patched_model) -> nn.Module:
+    """Turn `cpu_model` (an unpatched transformers Qwen2 model on the CPU, same
+    weights as `patched_model` before patching) into the reference's CPU path:
+    its projections take the int4 buffers of `patched_model`'s QuantLinears
+    (any device) and run dequantize-then-matmul. Modifies and returns cpu_model."""
+    model = cpu_model.to("cpu")
+    for layer, player in zip(model.model.layers, patched_model.model.layers):
+        for parent, pparent, names in ((layer.self_attn, player.self_attn, ("q_proj", "k_proj", "v_proj", "o_proj")),
+                                       (layer.mlp, player.mlp, ("gate_proj", "up_proj", "down_proj"))):
+            for name in names:
+                ql = getattr(pparent, name)
+                setattr(parent, name, OracleQuantLinear(
+                    ql.packed.cpu().numpy(), ql.scales.cpu(), ql.zeros.cpu(), ql.in_features,
+                    ql.out_features, None if ql.bias is None else ql.bias.cpu(), ql.group_size))
+        # norms stay transformers' RMSNorm; the MLP activation is the reference oracle
+        layer.mlp.forward = types.MethodType(_swiglu_mlp_forward, layer.mlp)
+    return model.eval()

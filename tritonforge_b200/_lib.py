@@ -48,6 +48,10 @@ SIGNATURES = {
     "tf_quantize_int4": (_i32, [_vp, _i64, _i64, _i32, _vp, _vp, _vp, _i32, _vp]),
     "tf_dequantize_int4": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i32, _vp]),
     "tf_unpack_int4": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "tf_rope_kv_append": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32,
+                                 _vp]),
+    "tf_decode_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _f32, _i32, _vp]),
+    "tf_swiglu_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
