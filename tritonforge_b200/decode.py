@@ -117,16 +117,16 @@ class QwenDecoder:
                 if not isinstance(lin, QuantLinear):
                     raise TypeError("QwenDecoder needs a model patched with quantize=True")
             self.layers.append({
-                "in_norm": layer.input_layernorm.weight,
-                "post_norm": layer.post_attention_layernorm.weight,
+                "in_norm": layer.input_layernorm.weight.detach(),
+                "post_norm": layer.post_attention_layernorm.weight.detach(),
                 "qkv": _cat_quant([a.q_proj, a.k_proj, a.v_proj]),
                 "o": a.o_proj,
                 "gu": _cat_quant([m.gate_proj, m.up_proj]),
                 "down": m.down_proj,
             })
-        self.final_norm = inner.norm.weight
-        self.embed = inner.embed_tokens.weight
-        self.lm_head = model.lm_head.weight
+        self.final_norm = inner.norm.weight.detach()
+        self.embed = inner.embed_tokens.weight.detach()
+        self.lm_head = model.lm_head.weight.detach()
         self.scale = self.D ** -0.5
         dev, dt, B = self.dev, self.dtype, batch
         # rotary tables [T, D] exactly as transformers computes them
@@ -164,6 +164,7 @@ class QwenDecoder:
     def _lin(self, x: torch.Tensor, ql: QuantLinear, out: torch.Tensor) -> torch.Tensor:
         return kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
 
+    @torch.no_grad()
     def step(self) -> torch.Tensor:
         """One decode step: consumes self.tokens at self.pos, writes the next
         tokens into self.tokens and advances self.pos (all on device)."""
@@ -204,6 +205,7 @@ class QwenDecoder:
         self.pos.add_(1)
         return self.tokens
 
+    @torch.no_grad()
     def capture(self) -> None:
         """Capture one decode step in a CUDA graph (after a warm-up step)."""
         s = torch.cuda.Stream(self.dev)
