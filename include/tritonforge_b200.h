@@ -88,6 +88,22 @@ int tf_qlinear_ex(const void* x, int64_t ldx, int x_dtype,
                   int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
                   void* workspace, size_t workspace_bytes, int regime, void* stream);
 
+/* tf_qlinear for callers that cannot allocate device memory (for example a
+ * plugin inside a framework whose allocator owns all device memory, or a host
+ * runtime behind an FFI with no CUDA allocator). No counterpart in the
+ * reference. The scratch comes from a 4 KiB array built into the library
+ * instead of a caller workspace; problems that need more are rejected with
+ * TF_ERR_WORKSPACE. The first call on each device sets the array up (looks up
+ * its device address, clears it on `stream`), so make it before any stream
+ * capture. All calls share the array: calls that can overlap on the GPU race,
+ * order them on one stream. Allocates nothing. */
+int tf_qlinear_noalloc(const void* x, int64_t ldx, int x_dtype,
+                       const uint8_t* packed, const void* scales, const void* zeros, int param_dtype,
+                       const void* bias, int bias_dtype,
+                       void* out, int64_t ldo,
+                       int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                       void* stream);
+
 /* Reads the device-side error word of a workspace (blocking copy on `stream`):
  * 0 when every kernel that used it completed its bounded waits. */
 int tf_workspace_error(const void* workspace, int* error_out, void* stream);

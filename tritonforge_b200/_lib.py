@@ -42,6 +42,8 @@ SIGNATURES = {
                           _i64, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
     "tf_qlinear_ex": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
                              _i64, _i64, _i64, _i64, _i32, _vp, _sz, _i32, _vp]),
+    "tf_qlinear_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
+                                  _i64, _i64, _i64, _i64, _i32, _vp]),
     "tf_workspace_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "tf_rmsnorm_residual": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _f32, _i32, _vp]),
     "tf_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp]),
