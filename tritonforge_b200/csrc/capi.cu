@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -61,6 +62,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     }
   });
   return fn;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("TRITONFORGE_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,

@@ -161,6 +161,14 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Programmatic dependent launch. Kernels launched with pdl=true may start
+// while the previous kernel in the stream is still running: each one calls
+// pdl_wait() before it reads or writes anything the previous kernel produces
+// or consumes, and pdl_trigger() once its own CTAs are resident so that the
+// next kernel can be scheduled early. Both are no-ops without PDL.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Named barrier among `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -183,5 +191,42 @@ int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void
 int encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                          const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3],
                          CUtensorMapSwizzle swizzle);
+
+// Whether kernels are launched with programmatic dependent launch (default on;
+// TRITONFORGE_B200_PDL=0 turns it off).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with an optional cluster shape and the PDL attribute.
+template <typename... KArgs, typename... Args>
+int launch_ex(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+              dim3 cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = cluster.x;
+    attrs[n].val.clusterDim.y = cluster.y;
+    attrs[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TF_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  }
+  return check_launch(what);
+}
 
 }  // namespace tf

@@ -34,6 +34,9 @@
 //    of the columns.
 // Every mbarrier wait is bounded (1 s); on expiry the kernel records an error
 // bit in the workspace header, drains its own in-flight copies and finishes.
+// With programmatic dependent launch the producer fetches the weights of its
+// first ring of stages before waiting for the previous kernel, so the weight
+// stream starts while the previous kernel is still finishing.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -228,6 +231,7 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
     fence_mbarrier_init();
   }
   __syncthreads();
+  pdl_trigger();
 
   const int g = lane >> 2;  // MMA group id: A row / B column
   const int q = lane & 3;   // thread in group
@@ -247,14 +251,28 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
       prefetch_tensormap(&smap);
       prefetch_tensormap(&zmap);
       const uint64_t pol = l2_policy_evict_first();
-      int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
+      // The weights do not depend on the previous kernel: fetch W, scales and
+      // zeros of the first ring's worth of stages before waiting for it (PDL),
+      // then the x slices of those stages.
+      const int pre = n_it < S ? n_it : S;
+      for (int it = 0; it < pre; ++it) {
+        uint8_t* st = smem + it * kStage;
+        const int stage = st_begin + it;
+        mbar_arrive_expect_tx(&full[it], (uint32_t)stage_tx_bytes(NT));
+        tma_load_2d_hint(st, &wmap, &full[it], n0, stage * kWRows, pol);
+        const int srow = (2 * stage) / args.rows_per_group;
+        tma_load_2d(st + s_off(NT), &smap, &full[it], n0, srow);
+        tma_load_2d(st + z_off(NT), &zmap, &full[it], n0, srow);
+      }
+      pdl_wait();
+      for (int it = 0; it < pre; ++it)
+        tma_load_3d(smem + it * kStage + x_off(), &xmap, &full[it], 0, 0, (st_begin + it) * (kStageK / 16));
+      int issued = pre;
+      for (int it = pre; it < n_it; ++it) {
         const int slot = it % S;
-        if (it >= S) {
-          if (!mbar_wait_bounded(&empty[slot], (uint32_t)(it / S - 1) & 1u, args.err, 1)) {
-            *abort_flag = 1;
-            break;
-          }
+        if (!mbar_wait_bounded(&empty[slot], (uint32_t)(it / S - 1) & 1u, args.err, 1)) {
+          *abort_flag = 1;
+          break;
         }
         if (*abort_flag) break;
         uint8_t* st = smem + slot * kStage;
@@ -372,6 +390,7 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
   const int rows = args.M < kMPad ? args.M : kMPad;
   const int tid = threadIdx.x;
   if (warp < WK) {
+    pdl_wait();  // output writes below must follow the previous kernel (PDL)
     named_barrier(1, kConsumers);
 #pragma unroll
     for (int a = 0; a < NT; ++a) {
@@ -486,21 +505,9 @@ static int launch_t(const gemv::Plan& p, const CUtensorMap* maps, const gemv::Ar
       return check_launch("gemv set smem attribute");
     attr_set[dev] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)p.n_cb, (unsigned)p.ksplit, 1);
-  cfg.blockDim = dim3(32 * (gemv::warps_k(NT) + 1), 1, 1);
-  cfg.dynamicSmemBytes = p.smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)p.ksplit;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = p.ksplit > 1 ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], a);
-  if (e != cudaSuccess) return fail(TF_ERR_CUDA, "gemv_int4 launch: %s", cudaGetErrorString(e));
-  return check_launch("gemv_int4");
+  return launch_ex("gemv_int4", kern, dim3((unsigned)p.n_cb, (unsigned)p.ksplit, 1),
+                   dim3(32 * (gemv::warps_k(NT) + 1), 1, 1), p.smem, st, dim3(1, (unsigned)p.ksplit, 1), maps[0],
+                   maps[1], maps[2], maps[3], a);
 }
 
 template <typename XT, typename PT>

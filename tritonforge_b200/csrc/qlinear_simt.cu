@@ -16,6 +16,8 @@ constexpr int kChunk = 64;  // k per shared-memory chunk
 template <typename XT>
 __global__ void __launch_bounds__(kCols) qlinear_simt_kernel(QLinearProblem pb) {
   __shared__ float xs[kRowsM][kChunk];
+  pdl_trigger();
+  pdl_wait();
   const int64_t n = (int64_t)blockIdx.x * kCols + threadIdx.x;
   const int64_t m0 = (int64_t)blockIdx.y * kRowsM;
   const XT* x = static_cast<const XT*>(pb.x);
@@ -72,9 +74,9 @@ __global__ void __launch_bounds__(kCols) qlinear_simt_kernel(QLinearProblem pb) 
 int simt_launch(const QLinearProblem& pb, cudaStream_t st) {
   if (cdiv(pb.M, kRowsM) > 65535) return fail(TF_ERR_BAD_SHAPE, "qlinear(simt): M too large");
   dim3 grid((unsigned)cdiv(pb.N, kCols), (unsigned)cdiv(pb.M, kRowsM));
-  if (pb.x_dtype == TF_F16) qlinear_simt_kernel<__half><<<grid, kCols, 0, st>>>(pb);
-  else qlinear_simt_kernel<__nv_bfloat16><<<grid, kCols, 0, st>>>(pb);
-  return check_launch("qlinear_simt");
+  if (pb.x_dtype == TF_F16)
+    return launch_ex("qlinear_simt", qlinear_simt_kernel<__half>, grid, dim3(kCols), 0, st, dim3(1, 1, 1), pb);
+  return launch_ex("qlinear_simt", qlinear_simt_kernel<__nv_bfloat16>, grid, dim3(kCols), 0, st, dim3(1, 1, 1), pb);
 }
 
 }  // namespace tf

@@ -40,6 +40,8 @@ template <typename T, typename TW, int VPT, bool HAS_RES, bool WRITE_SUM>
 __global__ void rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ r, const TW* __restrict__ w,
                                    T* __restrict__ normed, T* __restrict__ summed, int n, float eps) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int nvec = n >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * n);
@@ -100,6 +102,8 @@ template <typename T, typename TW, bool HAS_RES, bool WRITE_SUM>
 __global__ void rmsnorm_generic_kernel(const T* __restrict__ x, const T* __restrict__ r, const TW* __restrict__ w,
                                        T* __restrict__ normed, T* __restrict__ summed, int64_t n, float eps) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const T* xr = x + row * n;
   const T* rr = r + row * n;
@@ -144,18 +148,22 @@ int launch_rows(const void* x, const void* r, const void* w, void* normed, void*
     };
     const int ni = (int)n;
     if (nvec <= 1024) {
-      rmsnorm_vec_kernel<T, TW, 1, HR, WS><<<(unsigned)m, pick(1), 0, st>>>(xp, rp, wp, np_, sp, ni, eps);
+      return launch_ex("rmsnorm", rmsnorm_vec_kernel<T, TW, 1, HR, WS>, dim3((unsigned)m), dim3(pick(1)), 0, st,
+                       dim3(1, 1, 1), xp, rp, wp, np_, sp, ni, eps);
     } else if (nvec <= 2048) {
-      rmsnorm_vec_kernel<T, TW, 2, HR, WS><<<(unsigned)m, pick(2), 0, st>>>(xp, rp, wp, np_, sp, ni, eps);
+      return launch_ex("rmsnorm", rmsnorm_vec_kernel<T, TW, 2, HR, WS>, dim3((unsigned)m), dim3(pick(2)), 0, st,
+                       dim3(1, 1, 1), xp, rp, wp, np_, sp, ni, eps);
     } else if (nvec <= 4096) {
-      rmsnorm_vec_kernel<T, TW, 4, HR, WS><<<(unsigned)m, pick(4), 0, st>>>(xp, rp, wp, np_, sp, ni, eps);
+      return launch_ex("rmsnorm", rmsnorm_vec_kernel<T, TW, 4, HR, WS>, dim3((unsigned)m), dim3(pick(4)), 0, st,
+                       dim3(1, 1, 1), xp, rp, wp, np_, sp, ni, eps);
     } else {
-      rmsnorm_vec_kernel<T, TW, 8, HR, WS><<<(unsigned)m, pick(8), 0, st>>>(xp, rp, wp, np_, sp, ni, eps);
+      return launch_ex("rmsnorm", rmsnorm_vec_kernel<T, TW, 8, HR, WS>, dim3((unsigned)m), dim3(pick(8)), 0, st,
+                       dim3(1, 1, 1), xp, rp, wp, np_, sp, ni, eps);
     }
   } else {
-    rmsnorm_generic_kernel<T, TW, HR, WS><<<(unsigned)m, 256, 0, st>>>(xp, rp, wp, np_, sp, n, eps);
+    return launch_ex("rmsnorm", rmsnorm_generic_kernel<T, TW, HR, WS>, dim3((unsigned)m), dim3(256), 0, st,
+                     dim3(1, 1, 1), xp, rp, wp, np_, sp, n, eps);
   }
-  return check_launch("rmsnorm");
 }
 
 template <typename T, typename TW>

@@ -19,6 +19,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(const T* __restrict__ g, const T* __restrict__ u,
                                                           T* __restrict__ o, int64_t n_vec, int64_t numel) {
   constexpr int kVec = 16 / sizeof(T);
+  pdl_trigger();
+  pdl_wait();
   const uint4* g4 = reinterpret_cast<const uint4*>(g);
   const uint4* u4 = reinterpret_cast<const uint4*>(u);
   uint4* o4 = reinterpret_cast<uint4*>(o);
@@ -44,6 +46,8 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(const T* __restrict__ g
 template <typename T>
 __global__ void swiglu_scalar_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ o,
                                      int64_t numel) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
     o[i] = Num<T>::from_f(swiglu_f(g[i], u[i]));
@@ -60,13 +64,14 @@ int launch_swiglu(const void* g, const void* u, void* o, int64_t numel, cudaStre
     const int64_t n_vec = numel / (16 / (int64_t)sizeof(T));
     int64_t blocks = cdiv(n_vec > 0 ? n_vec : 1, threads);
     if (blocks > max_blocks) blocks = max_blocks;
-    swiglu_vec_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(gp, up, op, n_vec, numel);
+    return launch_ex("swiglu", swiglu_vec_kernel<T>, dim3((unsigned)blocks), dim3(threads), 0, st, dim3(1, 1, 1), gp,
+                     up, op, n_vec, numel);
   } else {
     int64_t blocks = cdiv(numel, threads);
     if (blocks > max_blocks) blocks = max_blocks;
-    swiglu_scalar_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(gp, up, op, numel);
+    return launch_ex("swiglu", swiglu_scalar_kernel<T>, dim3((unsigned)blocks), dim3(threads), 0, st,
+                     dim3(1, 1, 1), gp, up, op, numel);
   }
-  return check_launch("swiglu");
 }
 
 }  // namespace
