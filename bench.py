@@ -215,9 +215,11 @@ def run_reference(args) -> None:
 
 
 def _config(args) -> dict:
+    tp = args.model != "0.5b"
+    par = (f"tp{args.gpus}" if tp else f"replicas{args.gpus}") if args.gpus > 1 else "single"
     return {"workload": f"Qwen2.5-{args.model.upper()}-shaped int4 g128 greedy decode", "model": f"qwen2.5-{args.model}",
-            "batch_per_gpu": args.batch, "prompt_len": args.prompt, "global_batch": args.batch * args.gpus,
-            "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+            "batch_per_gpu": args.batch, "prompt_len": args.prompt,
+            "global_batch": args.batch if tp else args.batch * args.gpus, "parallelism": par,
             "weights": "int4 group-128 K-major (fp16 scales/zeros); embeddings/norms/lm_head fp16",
             "l2": "per-step working set (int4 weights + fp16 lm_head) exceeds the 126 MB L2"}
 
@@ -280,35 +282,33 @@ def run_ours(args) -> None:
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    args.want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
-    model, cpu_copy = build_model(args, dev)
-    vocab = model.config.vocab_size
-    prompt = prompt_ids(args, vocab, rank)
-    max_len = args.prompt + args.warmup + 2 * args.steps + 8
-    dec = QwenDecoder(model, batch=args.batch, max_len=max_len)
-    # prefill in chunks of M <= 32 rows so every projection runs the decode kernel
-    chunk = max(1, 32 // args.batch)
-    with torch.no_grad():
-        from transformers import DynamicCache
+    tp = args.model != "0.5b"
+    cpu_copy = model = None
+    if tp:
+        # tensor parallel over all ranks: synthetic seeded int4 shards generated on each rank
+        from tritonforge_b200.decode import QwenWeights
 
-        cache = DynamicCache()
-        for c0 in range(0, args.prompt, chunk):
-            out = model(prompt[:, c0:c0 + chunk].to(dev), past_key_values=cache, use_cache=True)
-            cache = out.past_key_values
-        from tritonforge_b200.decode import _layer_kv
-
-        for li in range(len(dec.layers)):
-            k, v = _layer_kv(cache, li)
-            dec.k_cache[li, :, :, :args.prompt].copy_(k)
-            dec.v_cache[li, :, :, :args.prompt].copy_(v)
-        dec.tokens.copy_(out.logits[:, -1, :].argmax(-1))
-        dec.pos.copy_(torch.tensor([args.prompt, args.prompt + 1], dtype=torch.int32))
-        del cache, out
+        args.want_cpu = False
+        weights = QwenWeights.synthetic(args.model, tp=world, rank=rank, dtype=torch.bfloat16, device=dev,
+                                        seed=0)
+        max_len = args.prompt + args.warmup + 2 * args.steps + 8
+        group = dist.group.WORLD if world > 1 else None
+        dec = QwenDecoder(weights, batch=args.batch, max_len=max_len, group=group)
+        dec.fill_cache(args.prompt, seed=1)
+    else:
+        args.want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
+        model, cpu_copy = build_model(args, dev)
+        vocab = model.config.vocab_size
+        prompt = prompt_ids(args, vocab, rank)
+        max_len = args.prompt + args.warmup + 2 * args.steps + 8
+        dec = QwenDecoder(model, batch=args.batch, max_len=max_len)
+        # prefill in chunks of M <= 32 rows so every projection runs the decode kernel
+        dec.prefill(prompt, chunk=max(1, 32 // args.batch))
     dec.capture()
     for _ in range(args.warmup):
         dec.replay()
     torch.cuda.synchronize(dev)
-    launches_per_step = 9 * len(dec.layers) + 1
+    launches_per_step = dec.launches_per_step()
 
     # ---- device-timed decode (tokens fed back on the device)
     if world > 1:
@@ -325,7 +325,8 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
-    value = world * args.batch * args.steps / (ms / 1000.0)
+    seqs = args.batch if tp else world * args.batch  # TP ranks decode the same sequences
+    value = seqs * args.steps / (ms / 1000.0)
 
     # ---- end to end: per step H2D of the input tokens (pinned) + D2H of the output tokens
     host_in = torch.empty(args.batch, dtype=torch.long, pin_memory=True)
@@ -347,7 +348,7 @@ def run_ours(args) -> None:
     f1.record(s)
     torch.cuda.synchronize(dev)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
-    e2e_value = world * args.batch * args.steps / (e2e_ms / 1000.0)
+    e2e_value = seqs * args.steps / (e2e_ms / 1000.0)
 
     peaks = _peaks()
     roof = gemv_roofline(dec, peaks["hbm_gbs"])
@@ -364,8 +365,11 @@ def run_ours(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random-init weights, random token ids)",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
+            "vs_baseline": None, "dtype": "bf16" if tp else "fp16",
+            "data": ("synthetic (random-init int4 weight shards; KV cache of the prompt length filled with random "
+                     "values in place of a prefill)") if tp else "synthetic (random-init weights, random token ids)",
             "config": _config(args), "clocks": clocks.summary(),
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": host_in.numel() * 8,
                     "d2h_bytes_per_step": host_out.numel() * 8},
@@ -374,6 +378,7 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    dec.release()
     del dec
     if world > 1:
         dist.barrier()
@@ -386,7 +391,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="0.5b", choices=["0.5b"])
+    ap.add_argument("--model", default="0.5b", choices=["0.5b", "7b", "72b"],
+                    help="0.5b: transformers model, replicas across GPUs; 7b/72b: tensor parallel across GPUs")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")

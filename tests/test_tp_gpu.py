@@ -1,0 +1,92 @@
+"""GPU tests of tensor-parallel decode: shards of the same int4 weights,
+decoded as TP ranks (threads on one GPU, or NCCL ranks on several GPUs),
+match a tp=1 decode of the full weights within the bf16 tolerance (2e-2 x RMS
+of the logits), and the ranks agree bit for bit."""
+
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+import threading
+
+import pytest
+import torch
+
+from tests.tp_check import ThreadReducer, copy_cache, logits_close
+from tritonforge_b200.decode import QwenDecoder, QwenWeights
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name,tp,layers", [("7b", 2, 2), ("72b", 4, 1), ("72b", 2, 1)])
+def test_tp_threads_match_tp1(name, tp, layers):
+    dev = torch.device("cuda", 0)
+    B, T, steps = 3, 64, 3
+    full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=11, layers=layers)
+    ref = QwenDecoder(full, B, T)
+    ref.fill_cache(20, seed=2)
+    red = ThreadReducer(tp)
+    decs = [QwenDecoder(full.shard(tp, r), B, T, group=red.member(r)) for r in range(tp)]
+    for r, d in enumerate(decs):
+        copy_cache(ref, d, tp, r)
+    widths = {d.I for d in decs}
+    if name == "72b":
+        assert len(widths) == 2  # 231 groups split unevenly
+    errors: list = []
+
+    def run(d):
+        try:
+            d.step()
+        except Exception as e:  # pragma: no cover - surfaced below
+            errors.append(e)
+            red.bar.abort()
+
+    for _ in range(steps):
+        ref.step()
+        threads = [threading.Thread(target=run, args=(d,)) for d in decs]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=300)
+        assert not errors, errors
+        torch.cuda.synchronize()
+        for d in decs[1:]:
+            assert torch.equal(d.buf["logits"], decs[0].buf["logits"])
+        ok, err, rms = logits_close(decs[0].buf["logits"], ref.buf["logits"])
+        assert ok, f"tp{tp} logits max-abs {err:.4g} > 2e-2 x RMS {rms:.4g}"
+        for d in decs:
+            d.tokens.copy_(ref.tokens)
+
+
+def test_shard_tp1_is_identity():
+    full = QwenWeights.synthetic("7b", tp=1, rank=0, dtype=torch.bfloat16, device=torch.device("cuda", 0),
+                                 seed=1, layers=1)
+    s = full.shard(1, 0)
+    for key in ("qkv", "o", "gu", "down"):
+        a, b = full.layers[0][key], s.layers[0][key]
+        assert torch.equal(a.packed, b.packed) and torch.equal(a.scales, b.scales)
+        assert torch.equal(a.zeros, b.zeros)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_nccl_matches_tp1():
+    n = 2 if torch.cuda.device_count() < 4 else 4
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(root, "tests", "tp_check.py")]
+    env = dict(os.environ, TP_CHECK_MODEL="72b" if n == 4 else "7b", TP_CHECK_LAYERS="1")
+    p = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
+    lines = [l for l in p.stdout.splitlines() if l.startswith("TP_CHECK ")]
+    assert p.returncode == 0 and lines, p.stdout[-3000:] + p.stderr[-3000:]
+    rep = json.loads(lines[-1][len("TP_CHECK "):])
+    assert rep["ok"] and rep["ranks_identical"], rep

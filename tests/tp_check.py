@@ -1,0 +1,116 @@
+"""Tensor-parallel decode checks shared by the GPU tests.
+
+`ThreadReducer` emulates TP ranks as threads on one GPU (host barrier, sum on
+device in the model dtype, like a 2-rank NCCL ring); run as a script under
+torchrun this module is the NCCL worker: every rank builds the same full
+weights, decodes its shard with the all-reduce captured in a CUDA graph, and
+rank 0 compares the logits with a tp=1 decode of the full weights.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+import threading
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from tritonforge_b200.decode import QwenDecoder, QwenWeights  # noqa: E402
+
+
+class ThreadReducer:
+    """In-place sum across `n` threads of one process (one thread per rank)."""
+
+    def __init__(self, n: int, timeout_s: float = 120.0):
+        self.n = n
+        self.slots: list = [None] * n
+        self.bar = threading.Barrier(n, timeout=timeout_s)
+
+    def member(self, rank: int) -> "_Member":
+        return _Member(self, rank)
+
+
+class _Member:
+    def __init__(self, red: ThreadReducer, rank: int):
+        self.red, self.rank = red, rank
+
+    def all_reduce(self, t: torch.Tensor) -> None:
+        red = self.red
+        torch.cuda.current_stream(t.device).synchronize()
+        red.slots[self.rank] = t
+        red.bar.wait()
+        if self.rank == 0:
+            acc = red.slots[0].clone()
+            for other in red.slots[1:]:
+                acc.add_(other)
+            for s in red.slots:
+                s.copy_(acc)
+            torch.cuda.current_stream(t.device).synchronize()
+        red.bar.wait()
+
+
+def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
+    """Give a TP rank the kv heads of `src`'s cache that it owns, and src's tokens/position."""
+    h = dst.Hkv
+    dst.k_cache.copy_(src.k_cache[:, :, rank * h:(rank + 1) * h])
+    dst.v_cache.copy_(src.v_cache[:, :, rank * h:(rank + 1) * h])
+    dst.tokens.copy_(src.tokens)
+    dst.pos.copy_(src.pos)
+
+
+def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> tuple[bool, float, float]:
+    err = float((got.float() - ref.float()).abs().max())
+    rms = float(ref.float().pow(2).mean().sqrt())
+    return err <= tol * rms, err, rms
+
+
+def _nccl_main() -> int:
+    import datetime
+
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    name = os.environ.get("TP_CHECK_MODEL", "7b")
+    layers = int(os.environ.get("TP_CHECK_LAYERS", "2"))
+    steps = int(os.environ.get("TP_CHECK_STEPS", "4"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    B, T = 4, 96
+    full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=3, layers=layers)
+    ref = QwenDecoder(full, B, T)
+    ref.fill_cache(40, seed=5)  # same seed on every rank -> same cache everywhere
+    dec = QwenDecoder(full.shard(world, rank), B, T, group=dist.group.WORLD)
+    copy_cache(ref, dec, world, rank)
+    report = {"rank": rank, "ok": True, "steps": []}
+    dec.capture()
+    for i in range(steps):
+        ref.step()
+        dec.graph.replay()
+        ok, err, rms = logits_close(dec.buf["logits"], ref.buf["logits"])
+        same_tok = bool(torch.equal(dec.tokens, ref.tokens))
+        report["steps"].append({"err": err, "rms": rms, "tokens_equal": same_tok})
+        report["ok"] &= ok
+        dec.tokens.copy_(ref.tokens)  # keep the two decodes on the same tokens
+    # ranks must agree bit for bit (replicated after the all-reduce)
+    gathered = [torch.empty_like(dec.buf["logits"]) for _ in range(world)]
+    dist.all_gather(gathered, dec.buf["logits"])
+    report["ranks_identical"] = all(torch.equal(gathered[0], g) for g in gathered)
+    report["ok"] &= report["ranks_identical"]
+    torch.cuda.synchronize()
+    dec.release()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print("TP_CHECK " + json.dumps(report), flush=True)
+    return 0 if report["ok"] else 1
+
+
+if __name__ == "__main__":
+    sys.exit(_nccl_main())

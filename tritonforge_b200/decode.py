@@ -93,30 +93,45 @@ def _cat_quant(lins: list[QuantLinear]) -> QuantLinear:
                        bias, lins[0].group_size)
 
 
-class QwenDecoder:
-    """Batch-B greedy decoder over a patched (int4 QuantLinear) Qwen2 model."""
+@dataclasses.dataclass
+class QwenWeights:
+    """Everything one rank needs to decode: per-layer int4 projections (with
+    q|k|v and gate|up concatenated along N), norms, embedding, lm_head and
+    rotary tables, with this rank's head / intermediate counts."""
 
-    def __init__(self, model, batch: int, max_len: int):
+    layers: list
+    embed: torch.Tensor
+    lm_head: torch.Tensor
+    final_norm: torch.Tensor
+    hidden: int
+    inter: int          # this rank's intermediate width
+    q_heads: int        # this rank's q heads
+    kv_heads: int       # this rank's kv heads
+    head_dim: int
+    eps: float
+    rope_theta: float
+    model: object = None  # the patched transformers model (prompt prefill), when there is one
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.embed.dtype
+
+    @classmethod
+    def from_hf(cls, model) -> "QwenWeights":
+        """From a transformers Qwen2 model patched with quantize=True."""
         cfg = model.config
-        self.model = model
-        self.B = batch
-        self.T = max_len
-        self.H = cfg.hidden_size
-        self.I = cfg.intermediate_size
-        self.Hq = cfg.num_attention_heads
-        self.Hkv = cfg.num_key_value_heads
-        self.D = getattr(cfg, "head_dim", None) or self.H // self.Hq
-        self.eps = cfg.rms_norm_eps
         inner = model.model
-        self.dev = inner.embed_tokens.weight.device
-        self.dtype = inner.embed_tokens.weight.dtype
-        self.layers = []
+        layers = []
         for layer in inner.layers:
             a, m = layer.self_attn, layer.mlp
             for lin in (a.q_proj, a.k_proj, a.v_proj, a.o_proj, m.gate_proj, m.up_proj, m.down_proj):
                 if not isinstance(lin, QuantLinear):
                     raise TypeError("QwenDecoder needs a model patched with quantize=True")
-            self.layers.append({
+            layers.append({
                 "in_norm": layer.input_layernorm.weight.detach(),
                 "post_norm": layer.post_attention_layernorm.weight.detach(),
                 "qkv": _cat_quant([a.q_proj, a.k_proj, a.v_proj]),
@@ -124,21 +139,125 @@ class QwenDecoder:
                 "gu": _cat_quant([m.gate_proj, m.up_proj]),
                 "down": m.down_proj,
             })
-        self.final_norm = inner.norm.weight.detach()
-        self.embed = inner.embed_tokens.weight.detach()
-        self.lm_head = model.lm_head.weight.detach()
+        return cls(layers, inner.embed_tokens.weight.detach(), model.lm_head.weight.detach(),
+                   inner.norm.weight.detach(), cfg.hidden_size, cfg.intermediate_size,
+                   cfg.num_attention_heads, cfg.num_key_value_heads,
+                   getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads,
+                   cfg.rms_norm_eps, getattr(cfg, "rope_theta", 1e6), model)
+
+    @classmethod
+    def synthetic(cls, name: str, tp: int = 1, rank: int = 0, dtype: torch.dtype = torch.bfloat16,
+                  device=None, seed: int = 0, layers: int | None = None) -> "QwenWeights":
+        """Random-init int4 weights of a Qwen2.5 shape, generated directly as
+        this rank's tensor-parallel shards (N(0, 0.02) fp32 per shard, int4 g128
+        quantised on the GPU; norms 1; embedding and lm_head replicated)."""
+        from .tp import TPLayout, synthetic_linear
+
+        shape = QWEN25[name]
+        lay = TPLayout(tp, rank, shape.hidden, shape.inter, shape.heads, shape.kv_heads, shape.head_dim)
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        H, D = shape.hidden, shape.head_dim
+        i0, i1 = lay.inter_cols
+        il = i1 - i0
+        nl = layers or shape.layers
+        out = []
+        for li in range(nl):
+            g = torch.Generator(device=device).manual_seed(seed * 1000003 + li * 131 + rank)
+            ones = torch.ones(H, dtype=dtype, device=device)
+            out.append({
+                "in_norm": ones,
+                "post_norm": ones,
+                "qkv": synthetic_linear((lay.q_heads + 2 * lay.kv_local) * D, H, g, device, dtype, bias=True),
+                "o": synthetic_linear(H, lay.q_heads * D, g, device, dtype),
+                "gu": synthetic_linear(2 * il, H, g, device, dtype),
+                "down": synthetic_linear(H, il, g, device, dtype),
+            })
+        g = torch.Generator(device=device).manual_seed(seed * 1000003 + 999_999)
+        embed = (torch.randn(shape.vocab, H, generator=g, device=device) * 0.02).to(dtype)
+        lm_head = embed if shape.tied else (torch.randn(shape.vocab, H, generator=g, device=device) * 0.02).to(dtype)
+        return cls(out, embed, lm_head, torch.ones(H, dtype=dtype, device=device), H, il, lay.q_heads,
+                   lay.kv_local, D, shape.eps, shape.rope_theta)
+
+
+    def shard(self, tp: int, rank: int) -> "QwenWeights":
+        """This rank's tensor-parallel shard of full (tp=1) weights: slices of
+        the quantised tensors, bit-identical to quantising the shard alone."""
+        from .tp import TPLayout, shard_cols, shard_rows
+
+        if self.q_heads % tp or self.kv_heads % tp:
+            raise ValueError(f"tp={tp} must divide q heads {self.q_heads} and kv heads {self.kv_heads}")
+        lay = TPLayout(tp, rank, self.hidden, self.inter, self.q_heads, self.kv_heads, self.head_dim)
+        D, I = self.head_dim, self.inter
+        nq, nkv = self.q_heads * D, self.kv_heads * D
+        (q0, q1), (k0, k1), (i0, i1) = lay.q_cols, lay.kv_cols, lay.inter_cols
+
+        def cols(ql: QuantLinear, spans) -> QuantLinear:
+            parts = [shard_cols(ql.packed, ql.scales, ql.zeros, ql.bias, a, b) for a, b in spans]
+            bias = None if ql.bias is None else torch.cat([p[3] for p in parts]).contiguous()
+            return QuantLinear(torch.cat([p[0] for p in parts], 1).contiguous(),
+                               torch.cat([p[1] for p in parts], 1).contiguous(),
+                               torch.cat([p[2] for p in parts], 1).contiguous(),
+                               ql.in_features, sum(b - a for a, b in spans), bias, ql.group_size)
+
+        def rows(ql: QuantLinear, a: int, b: int) -> QuantLinear:
+            p, s, z = shard_rows(ql.packed, ql.scales, ql.zeros, a, b, ql.group_size)
+            return QuantLinear(p, s, z, b - a, ql.out_features, ql.bias, ql.group_size)
+
+        layers = []
+        for L in self.layers:
+            layers.append({
+                "in_norm": L["in_norm"], "post_norm": L["post_norm"],
+                "qkv": cols(L["qkv"], [(q0, q1), (nq + k0, nq + k1), (nq + nkv + k0, nq + nkv + k1)]),
+                "o": rows(L["o"], q0, q1),
+                "gu": cols(L["gu"], [(i0, i1), (I + i0, I + i1)]),
+                "down": rows(L["down"], i0, i1),
+            })
+        return QwenWeights(layers, self.embed, self.lm_head, self.final_norm, self.hidden, i1 - i0,
+                           lay.q_heads, lay.kv_local, D, self.eps, self.rope_theta)
+
+
+def rotary_tables(w: QwenWeights, max_len: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_len, D] in the model dtype, as transformers' Qwen2 computes them."""
+    if w.model is not None:
+        inner = w.model.model
+        pos = torch.arange(max_len, device=w.device).unsqueeze(0)
+        probe = torch.zeros(1, 1, w.hidden, dtype=w.dtype, device=w.device)
+        cos, sin = inner.rotary_emb(probe, pos)
+        return cos[0].contiguous(), sin[0].contiguous()
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2RotaryEmbedding
+
+    cfg = hf_config(QwenShape(w.hidden, w.inter, 1, w.q_heads, w.kv_heads, w.head_dim, 1, w.eps, w.rope_theta))
+    rot = Qwen2RotaryEmbedding(cfg).to(w.device)
+    pos = torch.arange(max_len, device=w.device).unsqueeze(0)
+    cos, sin = rot(torch.zeros(1, 1, 8, dtype=w.dtype, device=w.device), pos)
+    return cos[0].contiguous(), sin[0].contiguous()
+
+
+class QwenDecoder:
+    """Batch-B greedy decoder over int4 Qwen2 weights (one rank of a
+    tensor-parallel group when `group` is given: the o_proj and down_proj
+    outputs are then partial sums, added across ranks by an all-reduce).
+    `group` is a torch.distributed process group, or any object with an
+    `all_reduce(tensor)` method that sums in place across the ranks."""
+
+    def __init__(self, model_or_weights, batch: int, max_len: int, group=None):
+        w = model_or_weights if isinstance(model_or_weights, QwenWeights) else QwenWeights.from_hf(model_or_weights)
+        self.w = w
+        self.model = w.model
+        self.group = group
+        self.B, self.T = batch, max_len
+        self.H, self.I = w.hidden, w.inter
+        self.Hq, self.Hkv, self.D = w.q_heads, w.kv_heads, w.head_dim
+        self.eps = w.eps
+        self.layers = w.layers
+        self.final_norm, self.embed, self.lm_head = w.final_norm, w.embed, w.lm_head
+        self.dev, self.dtype = w.device, w.dtype
         self.scale = self.D ** -0.5
         dev, dt, B = self.dev, self.dtype, batch
-        # rotary tables [T, D] exactly as transformers computes them
-        pos = torch.arange(max_len, device=dev).unsqueeze(0)
-        probe = torch.zeros(1, 1, self.H, dtype=dt, device=dev)
-        cos, sin = inner.rotary_emb(probe, pos)
-        self.cos = cos[0].contiguous()
-        self.sin = sin[0].contiguous()
+        self.cos, self.sin = rotary_tables(w, max_len)
         nl = len(self.layers)
         self.k_cache = torch.zeros(nl, B, self.Hkv, max_len, self.D, dtype=dt, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
-        # static step buffers
         nqkv = (self.Hq + 2 * self.Hkv) * self.D
         self.tokens = torch.zeros(B, dtype=torch.long, device=dev)
         self.pos = torch.zeros(2, dtype=torch.int32, device=dev)  # [position, length = position + 1]
@@ -163,6 +282,16 @@ class QwenDecoder:
     # ------------------------------------------------------------------ step
     def _lin(self, x: torch.Tensor, ql: QuantLinear, out: torch.Tensor) -> torch.Tensor:
         return kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        if self.group is None:
+            return
+        if hasattr(self.group, "all_reduce"):  # a reducer object (in-process ranks)
+            self.group.all_reduce(t)
+            return
+        import torch.distributed as dist
+
+        dist.all_reduce(t, group=self.group)
 
     @torch.no_grad()
     def step(self) -> torch.Tensor:
@@ -191,6 +320,7 @@ class QwenDecoder:
                 b["attn"].data_ptr(), lenp, self.B, self.Hq, self.Hkv, self.D, self.T, self.scale,
                 self._dt, st), "decode_attention")
             self._lin(b["attn"], L["o"], b["o"])
+            self._all_reduce(b["o"])
             kernels.rmsnorm_residual(b["o"], res, L["post_norm"], self.eps, out=(b["normed"], res_next))
             res, res_next = res_next, res
             self._lin(b["normed"], L["gu"], b["gu"])
@@ -199,30 +329,38 @@ class QwenDecoder:
                 gu.data_ptr(), gu.data_ptr() + self.I * gu.element_size(), b["act"].data_ptr(), self.B, self.I,
                 gu.stride(0), gu.stride(0), b["act"].stride(0), self._dt, st), "swiglu")
             self._lin(b["act"], L["down"], b["mlp"])
+            self._all_reduce(b["mlp"])
         kernels.rmsnorm_residual(b["mlp"], res, self.final_norm, self.eps, out=(b["normed"], res_next))
         torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
         torch.argmax(b["logits"], dim=-1, out=self.tokens)
         self.pos.add_(1)
         return self.tokens
 
+    def launches_per_step(self) -> int:
+        """Kernels of this library launched by one step."""
+        return 9 * len(self.layers) + 1
+
     @torch.no_grad()
     def capture(self) -> None:
         """Capture one decode step in a CUDA graph (after a warm-up step)."""
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
-        saved = (self.tokens.clone(), self.pos.clone(), self.k_cache.clone(), self.v_cache.clone())
+        saved = (self.tokens.clone(), self.pos.clone())
         with torch.cuda.stream(s):
             self.step()  # warm-up: sizes workspaces and sets kernel attributes outside capture
         torch.cuda.current_stream(self.dev).wait_stream(s)
+        # the warm-up appended at position `pos`, which the captured step overwrites
         self.tokens.copy_(saved[0])
         self.pos.copy_(saved[1])
-        self.k_cache.copy_(saved[2])
-        self.v_cache.copy_(saved[3])
         del saved
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             self.step()
         self.graph = g
+
+    def release(self) -> None:
+        """Drop the captured graph (before destroying a process group it uses)."""
+        self.graph = None
 
     def replay(self) -> torch.Tensor:
         if self.graph is None:
@@ -232,16 +370,28 @@ class QwenDecoder:
 
     # ---------------------------------------------------------------- prefill
     @torch.no_grad()
-    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
-        """Run the prompt [B, T0] through the patched model, copy its KV cache
-        into the static cache, and set the first generated tokens."""
+    def prefill(self, prompt: torch.Tensor, chunk: int | None = None) -> torch.Tensor:
+        """Run the prompt [B, T0] through the patched transformers model (in
+        chunks of `chunk` tokens when given), copy its KV cache into the static
+        cache, and set the first generated tokens."""
+        if self.model is None:
+            raise RuntimeError("prefill needs the transformers model; use fill_cache for synthetic weights")
         if prompt.shape[0] != self.B:
             raise ValueError(f"prompt batch {prompt.shape[0]} != decoder batch {self.B}")
         t0 = prompt.shape[1]
         if t0 >= self.T:
             raise ValueError(f"prompt length {t0} does not fit max_len {self.T}")
-        out = self.model(prompt.to(self.dev), use_cache=True)
-        cache = out.past_key_values
+        prompt = prompt.to(self.dev)
+        if chunk is None:
+            out = self.model(prompt, use_cache=True)
+            cache = out.past_key_values
+        else:
+            from transformers import DynamicCache
+
+            cache = DynamicCache()
+            for c0 in range(0, t0, chunk):
+                out = self.model(prompt[:, c0:c0 + chunk], past_key_values=cache, use_cache=True)
+                cache = out.past_key_values
         for li in range(len(self.layers)):
             k, v = _layer_kv(cache, li)
             self.k_cache[li, :, :, :t0].copy_(k)
@@ -249,6 +399,20 @@ class QwenDecoder:
         self.tokens.copy_(out.logits[:, -1, :].argmax(-1))
         self.pos.copy_(torch.tensor([t0, t0 + 1], dtype=torch.int32))
         return self.tokens.clone()
+
+    @torch.no_grad()
+    def fill_cache(self, length: int, seed: int = 0) -> None:
+        """Stand-in for a prompt prefill on synthetic weights: random K/V
+        (N(0, 1)) for the first `length` positions and random current tokens.
+        The decode steps that follow attend over all `length` positions."""
+        if length >= self.T:
+            raise ValueError(f"length {length} does not fit max_len {self.T}")
+        g = torch.Generator(device=self.dev).manual_seed(seed)
+        for li in range(len(self.layers)):
+            self.k_cache[li, :, :, :length].normal_(generator=g)
+            self.v_cache[li, :, :, :length].normal_(generator=g)
+        self.tokens.copy_(torch.randint(0, self.embed.shape[0], (self.B,), generator=g, device=self.dev))
+        self.pos.copy_(torch.tensor([length, length + 1], dtype=torch.int32))
 
     @torch.no_grad()
     def generate(self, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True) -> torch.Tensor:
