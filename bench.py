@@ -1,23 +1,31 @@
-"""Decode benchmark: Qwen2.5-shaped int4 model on the B200 kernels.
+"""Decode benchmark: Qwen2.5-shaped int4 models on the B200 kernels.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--model 0.5b] [--batch 8] [--prompt 128]
+                    [--model 72b|7b|0.5b] [--batch B] [--prompt T]
 
-Workload (default): the Qwen2.5-0.5B architecture, random init (seed 0, fp16),
-every q/k/v/o/gate/up/down an int4 group-128 QuantLinear, batch 8, prompts of
-128 uniform-random token ids, greedy decode. One step = one decoded token for
-each of the B sequences (all layers, lm_head, argmax), run as one CUDA graph.
+Default workload: the Qwen2.5-72B architecture (80 layers, hidden 8192, 64 q /
+8 kv heads of 128, intermediate 29568, vocab 152064), random-init int4
+group-128 weights (bf16 scales, zeros and activations), batch 32, a KV cache of
+4096 prompt positions filled with random values, greedy decode. The model is
+tensor-parallel over the N ranks (column-parallel q/k/v/gate/up, row-parallel
+o/down with an NCCL all-reduce after each, captured in the step's CUDA graph):
+total work is fixed as N grows (strong scaling). `--model 7b` is the 7B shape
+the same way; `--model 0.5b` is the transformers Qwen2.5-0.5B (fp16) patched
+with the int4 QuantLinear, prefilled through the model, one replica per rank.
+One step = one decoded token for each of the B sequences (all layers,
+lm_head, argmax).
 
-Prints one JSON line. `value` is decode tokens/s over all ranks, timed on the
-device (CUDA events, max over ranks) with tokens fed back on the device; `e2e`
-is the same metric through the decoder's public step with the step's input
-tokens copied from pinned host memory and its output tokens read back every
-step. With N > 1 every rank decodes its own batch (independent replicas: the
-0.5B model is not sharded). `roofline` is the int4 GEMV (the kernel that
-streams the weights), its launches of one step timed live on its stream.
-`cpu_baseline` times the reference's CPU path (transformers Qwen2 with the
-reference's dequantize-then-matmul QuantLinear, restated in oracle/) on a
-bounded sample of decode steps on this host's cores.
+Prints one JSON line. `value` is decode tokens/s of the whole job, timed on
+the device (CUDA events, max over ranks) with tokens fed back on the device;
+`e2e` is the same metric through the decoder's public step with the step's
+input tokens copied from pinned host memory and its output tokens read back
+every step. `roofline` is the int4 GEMV (the kernel that streams the
+weights): one step's GEMV launches replayed alone in a CUDA graph, algorithmic
+bytes / device time against the measured HBM copy bandwidth. `cpu_baseline`
+times the reference's CPU path (dequantize-then-matmul int4 projections,
+restated in oracle/) on this host's cores: for the 0.5B model whole decode
+steps, for 7B/72B one decoder layer plus the lm_head, extrapolated to all
+layers.
 
 `--impl reference` times that same CPU path as the reference arm (rank 0 only).
 """
@@ -183,31 +191,80 @@ def cpu_decode_rate(cpu_model, prompt, steps: int, budget_s: float) -> tuple[flo
     return b * done / dt, cores, done, sample
 
 
-def run_reference(args) -> None:
-    world, rank, _ = _dist()
-    if rank != 0:
-        return
+def cpu_layer_rate(args, dev, budget_s: float) -> tuple[float, int, str]:
+    """Decode tok/s of the reference's CPU path for a 7B/72B shape on this
+    host, from one decoder layer (timed over a few decode steps) plus the final
+    norm, lm_head and argmax, extrapolated to all layers."""
     import torch
 
-    from oracle.cpu_decode import cpu_reference_model
-    from tritonforge_b200.decode import random_qwen2
+    from oracle.cpu_decode import CpuLayer
+    from tritonforge_b200.decode import QWEN25, QwenWeights, rotary_tables
+
+    shape = QWEN25[args.model]
+    w = QwenWeights.synthetic(args.model, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=0, layers=1)
+    layer = CpuLayer(w.layers[0], w.hidden, w.q_heads, w.kv_heads, w.head_dim, w.eps)
+    t_max = args.prompt + 16
+    cos, sin = (t.cpu() for t in rotary_tables(w, t_max))
+    lm_head, final_norm = w.lm_head.cpu(), w.final_norm.cpu()
+    del w
+    torch.cuda.empty_cache()
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(5)
+    b = args.batch
+    x = torch.randn(b, shape.hidden, generator=g).to(torch.bfloat16)
+    kc = torch.randn(b, shape.kv_heads, t_max, shape.head_dim, generator=g).to(torch.bfloat16)
+    vc = torch.randn(b, shape.kv_heads, t_max, shape.head_dim, generator=g).to(torch.bfloat16)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        layer.step(x, kc, vc, args.prompt + n, cos, sin)
+        n += 1
+        if n >= 8 or time.perf_counter() - t0 > budget_s:
+            break
+    t_layer = (time.perf_counter() - t0) / n
+    t1 = time.perf_counter()
+    with torch.no_grad():
+        h = x.float()
+        h = (final_norm * (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + shape.eps)).to(x.dtype))
+        (h @ lm_head.t()).argmax(-1)
+    t_head = time.perf_counter() - t1
+    step_s = shape.layers * t_layer + t_head
+    sample = (f"1 of {shape.layers} decoder layers timed over {n} decode steps (batch {b}, context {args.prompt}) "
+              f"plus final norm/lm_head/argmax ({t_head:.2f} s), extrapolated to {shape.layers} layers: "
+              f"{step_s:.1f} s per step")
+    return b / step_s, cores, sample
+
+
+def run_reference(args) -> None:
+    # the reference's CPU path runs on rank 0 only; no process group is needed
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
 
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
     if dev is None:
         print(json.dumps({"impl": "reference", "unavailable": "needs a CUDA device to build the int4 weights"}))
         return
-    args.want_cpu = True
-    model, cpu_copy = build_model(args, dev)
-    cpu_model = cpu_reference_model(cpu_copy, model)
-    del model
-    torch.cuda.empty_cache()
-    prompt = prompt_ids(args, cpu_model.config.vocab_size, 0)
     budget = float(os.environ.get("TF_REF_BUDGET_S", "120"))
-    rate, cores, done, sample = cpu_decode_rate(cpu_model, prompt, args.steps, budget)
+    if args.model == "0.5b":
+        from oracle.cpu_decode import cpu_reference_model
+
+        args.want_cpu = True
+        model, cpu_copy = build_model(args, dev)
+        cpu_model = cpu_reference_model(cpu_copy, model)
+        del model
+        torch.cuda.empty_cache()
+        prompt = prompt_ids(args, cpu_model.config.vocab_size, 0)
+        rate, cores, done, sample = cpu_decode_rate(cpu_model, prompt, args.steps, budget)
+    else:
+        rate, cores, sample = cpu_layer_rate(args, dev, budget)
+        done = 0
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": done, "warmup": 0, "ms_per_step": 1000.0 * args.batch / rate, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random-init weights, random token ids)",
+        "scaling": "strong" if args.model != "0.5b" else "weak", "vs_baseline": None,
+        "dtype": "bf16" if args.model != "0.5b" else "fp16",
+        "data": "synthetic (random-init weights, random token ids / random KV cache)",
         "config": _config(args),
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -220,8 +277,9 @@ def _config(args) -> dict:
     return {"workload": f"Qwen2.5-{args.model.upper()}-shaped int4 g128 greedy decode", "model": f"qwen2.5-{args.model}",
             "batch_per_gpu": args.batch, "prompt_len": args.prompt,
             "global_batch": args.batch if tp else args.batch * args.gpus, "parallelism": par,
-            "weights": "int4 group-128 K-major (fp16 scales/zeros); embeddings/norms/lm_head fp16",
-            "l2": "per-step working set (int4 weights + fp16 lm_head) exceeds the 126 MB L2"}
+            "weights": ("int4 group-128 K-major, bf16 scales/zeros/activations; embedding, norms and lm_head bf16"
+                        if tp else "int4 group-128 K-major (fp16 scales/zeros); embeddings/norms/lm_head fp16"),
+            "l2": "per-step working set (int4 weights + lm_head) exceeds the 126 MB L2"}
 
 
 def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
@@ -355,11 +413,15 @@ def run_ours(args) -> None:
     roof["peak_source"] = peaks["source"]
 
     cpu = None
-    if rank == 0 and args.want_cpu:
-        from oracle.cpu_decode import cpu_reference_model
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if tp:
+            dec.release()
+            rate, cores, sample = cpu_layer_rate(args, dev, float(args.cpu_budget))
+        else:
+            from oracle.cpu_decode import cpu_reference_model
 
-        cpu_model = cpu_reference_model(cpu_copy, model)
-        rate, cores, _, sample = cpu_decode_rate(cpu_model, prompt, 1000, float(args.cpu_budget))
+            cpu_model = cpu_reference_model(cpu_copy, model)
+            rate, cores, _, sample = cpu_decode_rate(cpu_model, prompt, 1000, float(args.cpu_budget))
         cpu = {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -391,13 +453,17 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="0.5b", choices=["0.5b", "7b", "72b"],
-                    help="0.5b: transformers model, replicas across GPUs; 7b/72b: tensor parallel across GPUs")
-    ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--model", default="72b", choices=["72b", "7b", "0.5b"],
+                    help="72b/7b: tensor parallel across the GPUs; 0.5b: transformers model, one replica per GPU")
+    ap.add_argument("--batch", type=int, default=None, help="sequences (default 32 for 72b/7b, 8 for 0.5b)")
+    ap.add_argument("--prompt", type=int, default=None, help="context length (default 4096 / 2048 / 128)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.batch is None:
+        args.batch = 8 if args.model == "0.5b" else 32
+    if args.prompt is None:
+        args.prompt = {"72b": 4096, "7b": 2048, "0.5b": 128}[args.model]
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

@@ -74,3 +74,59 @@ def cpu_reference_model(cpu_model, patched_model) -> nn.Module:
         # norms stay transformers' RMSNorm; the MLP activation is the reference oracle
         layer.mlp.forward = types.MethodType(_swiglu_mlp_forward, layer.mlp)
     return model.eval()
+
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    # transformers' Qwen2RMSNorm: fp32 variance, cast back, times the weight
+    xf = x.float()
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * xf.to(x.dtype)
+
+
+def _rotate(t: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    half = t.shape[-1] // 2
+    rot = torch.cat((-t[..., half:], t[..., :half]), dim=-1)
+    return t * cos + rot * sin
+
+
+class CpuLayer:
+    """One Qwen2 decoder layer of int4 weights on the CPU, computed the
+    reference's way: dequantize-then-matmul projections (qwen.py:91-97),
+    transformers' RMSNorm, rotary embedding and scaled-dot-product attention
+    over the KV cache, the oracle SwiGLU (reference.py:53-57)."""
+
+    def __init__(self, layer: dict, hidden: int, q_heads: int, kv_heads: int, head_dim: int, eps: float):
+        def ql(q) -> OracleQuantLinear:
+            return OracleQuantLinear(q.packed.cpu().numpy(), q.scales.cpu(), q.zeros.cpu(), q.in_features,
+                                     q.out_features, None if q.bias is None else q.bias.cpu(), q.group_size)
+
+        self.qkv, self.o, self.gu, self.down = ql(layer["qkv"]), ql(layer["o"]), ql(layer["gu"]), ql(layer["down"])
+        self.in_norm, self.post_norm = layer["in_norm"].cpu(), layer["post_norm"].cpu()
+        self.H, self.Hq, self.Hkv, self.D, self.eps = hidden, q_heads, kv_heads, head_dim, eps
+        self.inter = self.gu.out_features // 2
+
+    @torch.no_grad()
+    def step(self, x: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: int,
+             cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """x [B, H] at position `pos`; caches [B, Hkv, T, D] hold positions < pos."""
+        b = x.shape[0]
+        h = _rms_norm(x, self.in_norm, self.eps)
+        qkv = self.qkv(h)
+        nq, nkv = self.Hq * self.D, self.Hkv * self.D
+        q = qkv[:, :nq].view(b, self.Hq, 1, self.D)
+        k = qkv[:, nq:nq + nkv].view(b, self.Hkv, 1, self.D)
+        v = qkv[:, nq + nkv:].view(b, self.Hkv, 1, self.D)
+        q, k = _rotate(q, cos[pos], sin[pos]), _rotate(k, cos[pos], sin[pos])
+        k_cache[:, :, pos:pos + 1] = k
+        v_cache[:, :, pos:pos + 1] = v
+        g = self.Hq // self.Hkv
+        kk = k_cache[:, :, :pos + 1].repeat_interleave(g, dim=1)
+        vv = v_cache[:, :, :pos + 1].repeat_interleave(g, dim=1)
+        attn = torch.nn.functional.scaled_dot_product_attention(q, kk, vv)
+        attn = attn.reshape(b, nq)
+        x = x + self.o(attn)
+        h = _rms_norm(x, self.post_norm, self.eps)
+        gu = self.gu(h).float()
+        gate, up = gu[:, :self.inter], gu[:, self.inter:]
+        act = ((gate * torch.sigmoid(gate)) * up).to(x.dtype)
+        return x + self.down(act)

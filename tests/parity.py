@@ -29,7 +29,11 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 
 def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, what: str = "",
-                     max_mismatch: float | None = None) -> dict:
+                     max_mismatch: float | None = None, mean_frac: float | None = 0.1) -> dict:
+    """max-abs error <= RMS_TOL x RMS(ref) (the contract); optionally at most
+    `max_mismatch` of the elements differ from the oracle at all, and the mean
+    abs error is at most `mean_frac` of the max-abs tolerance (typical errors
+    are ulp-level, not just bounded)."""
     got = f32(out)
     ref = np.asarray(ref, np.float32)
     assert got.shape == ref.shape, (got.shape, ref.shape)
@@ -41,9 +45,12 @@ def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, wha
     assert np.isfinite(got).all(), f"{what}: non-finite output"
     assert err <= tol, f"{what}: max-abs {err:.4g} > {RMS_TOL[dtype]} x RMS {rms:.4g}"
     mism = float(np.mean(got != ref))
+    mean_err = float(np.mean(np.abs(got.astype(np.float64) - ref.astype(np.float64))))
+    if mean_frac is not None:
+        assert mean_err <= mean_frac * tol, f"{what}: mean abs error {mean_err:.4g} > {mean_frac} x {tol:.4g}"
     if max_mismatch is not None:
         assert mism <= max_mismatch, f"{what}: {mism:.3%} of elements differ from the oracle"
-    return {"max_abs": err, "rms": rms, "mismatch": mism}
+    return {"max_abs": err, "rms": rms, "mismatch": mism, "mean_abs": mean_err}
 
 
 def oracle_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,

@@ -39,7 +39,7 @@ def test_quantized_linear_reference_shapes(m, n, k, dtype):
     x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype)
     out = kernels.quantized_linear(x, packed, scales, zeros, b)
     ref = oracle_linear(x, packed, scales, zeros, b)
-    assert_rms_close(out, ref, dtype, f"qlinear {m}x{n}x{k}", max_mismatch=0.02)
+    assert_rms_close(out, ref, dtype, f"qlinear {m}x{n}x{k}")
 
 
 DECODE_SHAPES = [(896, 4864), (4864, 896), (896, 896), (896, 128),
@@ -55,7 +55,7 @@ def test_gemv_decode_shapes(m, k, n, dtype):
     x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, bias=(n != 512), seed=m + n)
     out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemv"})
     ref = oracle_linear(x, packed, scales, zeros, b)
-    assert_rms_close(out, ref, dtype, f"gemv {m}x{n}x{k}", max_mismatch=0.02)
+    assert_rms_close(out, ref, dtype, f"gemv {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("regime", ["gemv", "simt"])
@@ -66,7 +66,7 @@ def test_mixed_param_dtype(regime, xdt, pdt):
     b = b.to(pdt)
     out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": regime})
     ref = oracle_linear(x, packed, scales, zeros, b)
-    assert_rms_close(out, ref, xdt, "mixed", max_mismatch=0.02)
+    assert_rms_close(out, ref, xdt, "mixed")
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -80,13 +80,13 @@ def test_simt_regime(m, n, k, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("k,regime", [(192, "gemv"), (200, "auto"), (1168, "gemv")])
+@pytest.mark.parametrize("k,regime", [(192, "gemv"), (200, "auto"), (1216, "gemv"), (1168, "auto")])
 def test_x_shorter_than_packed_k(k, regime, dtype):
     # K < K_pad: the kernels read x[:, K:] as zeros (the reference pads x)
     x, packed, scales, zeros, b = _linear_inputs(4, 1024, k, dtype, w_std=0.02, seed=3)
     out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": regime})
     ref = oracle_linear(x, packed, scales, zeros, b)
-    assert_rms_close(out, ref, dtype, f"K={k} < K_pad", max_mismatch=0.02)
+    assert_rms_close(out, ref, dtype, f"K={k} < K_pad")
 
 
 def test_no_bias_fp32_bias_and_strided_x():
@@ -100,7 +100,7 @@ def test_no_bias_fp32_bias_and_strided_x():
     wide = torch.zeros(4, 1536, dtype=torch.float16, device="cuda")
     wide[:, :1024] = x
     out = kernels.quantized_linear(wide[:, :1024], packed, scales, zeros)  # row stride 1536
-    assert_rms_close(out, ref, torch.float16, "strided x", max_mismatch=0.02)
+    assert_rms_close(out, ref, torch.float16, "strided x")
 
 
 def test_empty_and_determinism():
@@ -125,7 +125,7 @@ def test_large_m_rows_sampled(dtype):
     out = kernels.quantized_linear(x, packed, scales, zeros, b)
     rows = torch.randperm(m, generator=torch.Generator().manual_seed(0))[:64].sort().values
     ref = oracle_linear(x[rows.cuda()], packed, scales, zeros, b)
-    assert_rms_close(out[rows.cuda()], ref, dtype, "prefill rows", max_mismatch=0.02)
+    assert_rms_close(out[rows.cuda()], ref, dtype, "prefill rows")
 
 
 def test_golden_linear_cases():
@@ -140,7 +140,7 @@ def test_golden_linear_cases():
         b = (torch.from_numpy(gio.get_f32(rec, f"{case}/bias")).to(dt).cuda()
              if gio.has(rec, f"{case}/bias") else None)
         out = kernels.quantized_linear(x, packed, s, z, b)
-        assert_rms_close(out, gio.get_f32(rec, f"{case}/out"), dt, case, max_mismatch=0.05)
+        assert_rms_close(out, gio.get_f32(rec, f"{case}/out"), dt, case)
 
 
 # ---- rmsnorm_residual / rmsnorm ---------------------------------------------

@@ -157,3 +157,43 @@ def test_rank_exit_fails_cleanly_on_host():
         if p.is_alive():
             p.kill()
     assert rank == 0 and status.startswith("failed"), status
+
+
+def _argmax_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from tritonforge_b200.tp import best_of_ranks, local_best
+
+        g = torch.Generator().manual_seed(11)
+        vocab, b = 1001, 6
+        logits = torch.randint(-4, 5, (b, vocab), generator=g).to(torch.bfloat16)  # many ties
+        logits[0, 3] = 9.0
+        logits[0, 700] = 9.0   # tie across ranks: the smaller id must win
+        logits[1, :] = 0.0     # all equal: id 0
+        v0, v1 = split_even(vocab, world, rank)
+        best = torch.empty(b, 2)
+        arg = torch.empty(b, dtype=torch.long)
+        local_best(logits[:, v0:v1].contiguous(), v0, best, arg)
+        all_best = torch.empty(world, b, 2)
+        dist.all_gather_into_tensor(all_best.view(-1, 2), best)
+        tok = best_of_ranks(all_best).long()
+        q.put((rank, bool(torch.equal(tok, torch.argmax(logits, dim=-1))), tok.tolist()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_parallel_argmax_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, info in results:
+        assert ok, (rank, info)

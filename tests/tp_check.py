@@ -64,8 +64,14 @@ def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
 
 
 def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> tuple[bool, float, float]:
-    err = float((got.float() - ref.float()).abs().max())
-    rms = float(ref.float().pow(2).mean().sqrt())
+    """max |got - ref| <= tol x RMS(ref), after allowing each element one ulp
+    of its own bf16 rounding (row-parallel partial sums are rounded to bf16
+    before the all-reduce adds them, so a logit of magnitude 8 may differ by
+    its ulp, 0.0625, which is 5% of an RMS near 1.2)."""
+    ref32 = ref.float()
+    ulp = torch.ldexp(torch.ones_like(ref32), torch.frexp(ref32)[1] - 8)  # bf16 ulp of each value
+    err = float(((got.float() - ref32).abs() - ulp).clamp_min(0).max())
+    rms = float(ref32.pow(2).mean().sqrt())
     return err <= tol * rms, err, rms
 
 
@@ -90,18 +96,26 @@ def _nccl_main() -> int:
     copy_cache(ref, dec, world, rank)
     report = {"rank": rank, "ok": True, "steps": []}
     dec.capture()
+    v0, nv = dec.v0, dec.lm_head.shape[0]  # this rank's vocabulary slice (vocab-parallel lm_head)
+    same_all = True
     for i in range(steps):
         ref.step()
         dec.graph.replay()
-        ok, err, rms = logits_close(dec.buf["logits"], ref.buf["logits"])
+        ok, err, rms = logits_close(dec.buf["logits"], ref.buf["logits"][:, v0:v0 + nv])
         same_tok = bool(torch.equal(dec.tokens, ref.tokens))
+        if not same_tok:
+            # allowed only where the reference's best two logits are within the tolerance
+            top2 = ref.buf["logits"].float().topk(2, dim=-1).values
+            gap = float((top2[:, 0] - top2[:, 1])[dec.tokens != ref.tokens].min())
+            ok &= gap <= 2e-2 * rms
         report["steps"].append({"err": err, "rms": rms, "tokens_equal": same_tok})
         report["ok"] &= ok
+        # ranks must agree on the tokens bit for bit
+        gathered = [torch.empty_like(dec.tokens) for _ in range(world)]
+        dist.all_gather(gathered, dec.tokens)
+        same_all &= all(torch.equal(gathered[0], g) for g in gathered)
         dec.tokens.copy_(ref.tokens)  # keep the two decodes on the same tokens
-    # ranks must agree bit for bit (replicated after the all-reduce)
-    gathered = [torch.empty_like(dec.buf["logits"]) for _ in range(world)]
-    dist.all_gather(gathered, dec.buf["logits"])
-    report["ranks_identical"] = all(torch.equal(gathered[0], g) for g in gathered)
+    report["ranks_identical"] = same_all
     report["ok"] &= report["ranks_identical"]
     torch.cuda.synchronize()
     dec.release()

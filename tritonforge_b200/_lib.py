@@ -124,11 +124,13 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 class _Workspaces:
-    """Per-device zero-initialised scratch for split-K partials and tickets.
+    """Per-device zero-initialised scratch handed to the kernels (its header
+    holds the device error word of the bounded waits; the kernels keep no other
+    state in it).
 
-    Kernels leave their ticket counters at zero, so a buffer is zeroed only when
-    it is (re)allocated. Reallocation happens outside any CUDA-graph capture:
-    callers that capture size it first with ``reserve``.
+    A buffer is zeroed only when it is (re)allocated. Reallocation happens
+    outside any CUDA-graph capture: callers that capture size it first with
+    ``reserve``.
     """
 
     def __init__(self) -> None:

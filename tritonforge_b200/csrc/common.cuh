@@ -96,6 +96,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is
+// incomplete (it returns as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and sets `err_bits` in
 // the device error word) when the phase did not complete within `limit_ns`.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: kernels here run for microseconds
@@ -105,7 +119,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
     if (globaltimer_ns() - t0 > limit_ns) {
       if (err_word) atomicOr(err_word, err_bits);
       return false;
@@ -113,7 +127,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// 2-D tiled TMA load (no multicast), completion signalled on `bar`.
+// 2-D tiled TMA load into this CTA's shared memory, completion signalled on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1) {
   asm volatile(
@@ -133,7 +147,7 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
-// 3-D tiled TMA load (no multicast), completion signalled on `bar`.
+// 3-D tiled TMA load into this CTA's shared memory, completion signalled on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2) {
   asm volatile(

@@ -4,28 +4,30 @@
 // (src/tritonforge/kernels/dequant_gemm.py:39-113) for small M, where the op is
 // bound by streaming the packed weights from HBM.
 //
-// Structure (one CTA = WK consumer warps + 1 producer warp, 128 output columns):
+// Structure (one CTA = 8 consumer warps + 1 producer warp, 128 output columns):
 //  * Work unit = a stage of 256 k (two 128-k groups). Grid = [N/128 column
 //    blocks, ksplit]; a CTA owns a contiguous range of stages of its column
-//    block. Consumer warps work in pairs: pair p takes every (WK/2)-th stage
-//    and each warp of the pair one of its two groups, so every warp processes
-//    whole groups and the stages of a CTA are consumed concurrently.
-//  * The producer issues 4 TMA operations per stage (the per-SM TMA engine is
-//    limited by operations in flight, so each carries as many bytes as
-//    possible): the packed tile [128 rows x 128 B] (16 KiB, 128-byte swizzle,
-//    L2 evict-first), the x slice [M_pad x 256 k] as one 3-D box laid out
-//    [16-k chunk][row][16 k] (conflict-free B-fragment reads), and the two
-//    scale/zero rows of the stage.
-//  * Consumer warps dequantise in registers with the reference's rounding:
-//    w = round_x((code - zero) * scale). Nibbles become halves with one lop3
-//    against a magic exponent (1024+c / 64+c for fp16, 128+c for bf16); the
-//    subtraction is exact and `mul.rn` rounds once, so every dequantised
-//    weight equals the oracle's bit for bit.
-//  * Dot products run on the tensor pipe with mma.sync m16n8k16: dequantised
-//    weights are the A operand (16 output columns x 16 k), x^T is B (16 k x 8
-//    tokens), fp32 accumulators. The k order inside each 16-k step is permuted
-//    identically for A and B so one byte pair from two packed rows fills one A
-//    register without shuffles.
+//    block. A stage splits into 4 warp units (group h x 64-column half c);
+//    12 consumer warps (3 per SM sub-partition) take unit w % 4 of every third
+//    stage, so three stages are being consumed at a time and the rest of the
+//    ring keeps copies in flight.
+//  * The producer issues 4 TMA operations per stage. The TMA engine's cost
+//    grows with the number of lines (rows of a box) it moves, so each copy
+//    uses 128-byte lines: the packed tile [128 rows x 128 B] (16 KiB, 128-byte
+//    swizzle, L2 evict-first), the x slice [M rows x 256 k] as a 3-D box of
+//    4 x M lines of 64 k (128-byte swizzle: conflict-free B-fragment reads),
+//    and the two scale/zero rows of the stage.
+//  * Consumers dequantise exactly as the reference does (reference.py:21-35,
+//    quant.py:90-105): w = round_x((code - zero) * scale). A nibble becomes the
+//    half (O + code) with one lop3 against a magic exponent (O = 1024 / 64 for
+//    fp16, 128 for bf16); subtracting (O + zero) is exact and the multiply by
+//    the scale rounds once, so every weight equals the oracle's bit for bit.
+//    (When x and the scales have different types, the same value is formed in
+//    fp32 and rounded once to x's type.) Dot products run on the tensor pipe
+//    with mma.sync m16n8k16: weights are the A operand (16 output columns x
+//    16 k), x^T is B (16 k x 8 tokens), fp32 accumulators. The k order inside
+//    each 16-k step is permuted identically for A and B so one byte pair from
+//    two packed rows fills one A register without shuffles.
 //  * Reduction: the warps' partial sums are added in shared memory (fixed
 //    order); the ksplit CTAs of a column block form a thread-block cluster and
 //    add their partials through distributed shared memory (fixed rank order),
@@ -52,20 +54,24 @@ constexpr int kStageK = 256;               // k per stage (two groups of 128)
 constexpr int kWRows = kStageK / 2;        // packed rows per stage
 constexpr int kWBoxBytes = kWRows * kCols; // 16 KiB
 constexpr int kMaxCluster = 8;
-
-__host__ __device__ constexpr int warps_k(int nt) { return 4; }
-__host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 4 ? 1 : 2; }
-constexpr int kPairs = 2;  // consumer warp pairs per CTA (warps_k / 2)
-__host__ __device__ constexpr int x_chunk_bytes(int nt) { return 8 * nt * 32; }  // one 16-k chunk, all rows
-__host__ __device__ constexpr int x_off() { return kWBoxBytes; }
-__host__ __device__ constexpr int s_off(int nt) { return x_off() + 16 * x_chunk_bytes(nt); }
-__host__ __device__ constexpr int z_off(int nt) { return s_off(nt) + 2 * kCols * 2; }
-__host__ __device__ constexpr int stage_tx_bytes(int nt) { return z_off(nt) + 2 * kCols * 2; }
-__host__ __device__ constexpr int stage_bytes(int nt) { return (stage_tx_bytes(nt) + 1023) / 1024 * 1024; }
 constexpr int kRedPitch = kCols + 4;       // floats per row of the smem reduction tiles
-__host__ __device__ constexpr int red_bytes(int nt) {
-  return (warps_k(nt) + 1) * 8 * nt * kRedPitch * 4;  // per-warp tiles + the CTA tile
-}
+constexpr int kWarps = 12;                 // consumer warps per CTA
+constexpr int kCW = 64;                    // columns of one warp unit
+constexpr int kSpan = kCW / 8;             // packed bytes (columns) per thread and row
+constexpr int kTiles = kCW / 16;           // 16-column MMA tiles of a unit
+constexpr int kUnits = 2 * (kCols / kCW);  // warp units per stage
+constexpr int kStep = kWarps / kUnits;     // stages between two units of one warp
+
+template <int NT>
+struct Cfg {
+  static constexpr int kMPad = 8 * NT;            // token rows (M padded to the MMA n = 8)
+  static constexpr int kXOff = kWBoxBytes;        // x lines [4 chunks of 64 k][M_pad rows][128 B]
+  static constexpr int kSOff = kXOff + 4 * kMPad * 128;
+  static constexpr int kZOff = kSOff + 2 * kCols * 2;
+  static constexpr int kEnd = kZOff + 2 * kCols * 2;
+  static constexpr int kStage = (kEnd + 1023) / 1024 * 1024;
+  static constexpr int kRed = (kWarps + 1) * kMPad * kRedPitch * 4;  // per-warp tiles + the CTA tile
+};
 
 struct Args {
   const void* bias;
@@ -77,39 +83,42 @@ struct Args {
   int n_chunks;         // K_pad / 128
   int stages_per_cta;
   int ksplit;           // CTAs per cluster along K
-  int rows_per_group;   // group_size / 128
+  int rows_per_group;   // group_size / 128 (1: each 128-k chunk is its own group)
   int bias_dtype;
   int S;                // ring depth
+  uint32_t tx_bytes;    // bytes the four copies of a stage deliver
 };
 
+// Nibble -> (offset + code) halves, exact dequantisation and the MMA.
 template <typename T> struct Ops;
 
 template <> struct Ops<__half> {
-  static constexpr uint32_t kMagicLo = 0x64006400u;  // 1024 + nibble (bits 0..3)
-  static constexpr uint32_t kMagicHi = 0x54005400u;  // 64 + nibble (bits 4..7)
-  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, kMagicLo); }
-  static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t, 0x00F000F0u, kMagicHi); }
-  static constexpr uint32_t kOffLo2 = 0x64006400u, kOffHi2 = 0x54005400u;  // (1024, 1024), (64, 64)
+  // lo: nibbles at bits 0..3 of each half -> 1024 + c; hi: bits 4..7 -> 64 + c
+  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, 0x64006400u); }
+  static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t, 0x00F000F0u, 0x54005400u); }
+  static constexpr float kOffLo = 1024.0f, kOffHi = 64.0f;
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
   static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
-  // a (op) broadcast(lane of pair), round-to-nearest-even
-  static __device__ __forceinline__ uint32_t sub_l(uint32_t a, uint32_t pair, int lane) {
-    __half2 x = *reinterpret_cast<__half2*>(&a), p = *reinterpret_cast<__half2*>(&pair);
-    __half2 r = __hsub2(x, lane ? __high2half2(p) : __low2half2(p));
-    return *reinterpret_cast<uint32_t*>(&r);
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
   }
-  // a (op) broadcast(lane of pair), round-to-nearest-even
-  static __device__ __forceinline__ uint32_t mul_l(uint32_t a, uint32_t pair, int lane) {
-    __half2 x = *reinterpret_cast<__half2*>(&a), p = *reinterpret_cast<__half2*>(&pair);
-    __half2 r = __hmul2(x, lane ? __high2half2(p) : __low2half2(p));
-    return *reinterpret_cast<uint32_t*>(&r);
+  static __device__ __forceinline__ uint32_t splat(float v) {
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
   }
   static __device__ __forceinline__ uint32_t pack2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
   }
   static __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm(
@@ -121,30 +130,36 @@ template <> struct Ops<__half> {
 };
 
 template <> struct Ops<__nv_bfloat16> {
-  static constexpr uint32_t kMagic = 0x43004300u;  // 128 + nibble (bits 0..3)
-  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, kMagic); }
-  static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t >> 4, 0x000F000Fu, kMagic); }
-  static constexpr uint32_t kOffLo2 = 0x43004300u, kOffHi2 = 0x43004300u;  // (128, 128)
+  // both nibbles -> 128 + c (bf16 has no room for a nibble at bits 4..7)
+  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, 0x43004300u); }
+  // t >> 4 as the high word of t * 2^28: an integer multiply, which runs on
+  // the FMA pipe and leaves the (half-rate) ALU pipe to the lop3/prmt work
+  static __device__ __forceinline__ uint32_t hi(uint32_t t) {
+    return lop3_and_or(__umulhi(t, 0x10000000u), 0x000F000Fu, 0x43004300u);
+  }
+  static constexpr float kOffLo = 128.0f, kOffHi = 128.0f;
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
   static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
-  // a (op) broadcast(lane of pair), round-to-nearest-even
-  static __device__ __forceinline__ uint32_t sub_l(uint32_t a, uint32_t pair, int lane) {
-    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a), p = *reinterpret_cast<__nv_bfloat162*>(&pair);
-    __nv_bfloat162 r = __hsub2(x, lane ? __high2bfloat162(p) : __low2bfloat162(p));
-    return *reinterpret_cast<uint32_t*>(&r);
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
   }
-  // a (op) broadcast(lane of pair), round-to-nearest-even
-  static __device__ __forceinline__ uint32_t mul_l(uint32_t a, uint32_t pair, int lane) {
-    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a), p = *reinterpret_cast<__nv_bfloat162*>(&pair);
-    __nv_bfloat162 r = __hmul2(x, lane ? __high2bfloat162(p) : __low2bfloat162(p));
-    return *reinterpret_cast<uint32_t*>(&r);
+  static __device__ __forceinline__ uint32_t splat(float v) {
+    const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    return h | (h << 16);
   }
   static __device__ __forceinline__ uint32_t pack2(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
   }
   static __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm(
@@ -188,25 +203,22 @@ __device__ __forceinline__ void add4(float4& v, const float4& f) {
 }
 
 template <typename XT, typename PT, int NT>
-__global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
+__global__ void __launch_bounds__(32 * (kWarps + 1), 1)
     gemv_int4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                      const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
                      const Args args) {
-  constexpr int WK = warps_k(NT);
-  static_assert(WK == 2 * kPairs, "consumer warps come in pairs");
-  constexpr bool kExact = std::is_same<XT, PT>::value;  // dequant in half2 with exact rounding
-  constexpr int kMPad = 8 * NT;
-  constexpr int kXChunk = x_chunk_bytes(NT);
-  constexpr int kStage = stage_bytes(NT);
-  constexpr int kConsumers = WK * 32;
+  using C = Cfg<NT>;
+  constexpr int kMPad = C::kMPad;
+  constexpr bool kSameType = std::is_same<XT, PT>::value;
+  constexpr int kConsumers = kWarps * 32;
   using O = Ops<XT>;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
   const int S = args.S;
-  int ring = S * kStage;
-  if (ring < red_bytes(NT)) ring = red_bytes(NT);
+  int ring = S * C::kStage;
+  if (ring < C::kRed) ring = C::kRed;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
@@ -225,7 +237,7 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 2);  // the two warps of a pair
+      mbar_init(&empty[i], kUnits);  // one arrival per warp unit of the stage
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -235,15 +247,16 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
 
   const int g = lane >> 2;  // MMA group id: A row / B column
   const int q = lane & 3;   // thread in group
-  float acc[NT][8][4];
+  // per-thread totals: [token tile][column tile][C fragment]
+  float acc[NT][kTiles][4];
 #pragma unroll
   for (int a = 0; a < NT; ++a)
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
+    for (int t = 0; t < kTiles; ++t)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[a][t][e] = 0.0f;
 
-  if (warp == WK) {
+  if (warp == kWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tensormap(&wmap);
@@ -256,34 +269,39 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
       // then the x slices of those stages.
       const int pre = n_it < S ? n_it : S;
       for (int it = 0; it < pre; ++it) {
-        uint8_t* st = smem + it * kStage;
+        uint8_t* st = smem + it * C::kStage;
         const int stage = st_begin + it;
-        mbar_arrive_expect_tx(&full[it], (uint32_t)stage_tx_bytes(NT));
+        mbar_arrive_expect_tx(&full[it], args.tx_bytes);
         tma_load_2d_hint(st, &wmap, &full[it], n0, stage * kWRows, pol);
         const int srow = (2 * stage) / args.rows_per_group;
-        tma_load_2d(st + s_off(NT), &smap, &full[it], n0, srow);
-        tma_load_2d(st + z_off(NT), &zmap, &full[it], n0, srow);
+        tma_load_2d(st + C::kSOff, &smap, &full[it], n0, srow);
+        tma_load_2d(st + C::kZOff, &zmap, &full[it], n0, srow);
       }
       pdl_wait();
       for (int it = 0; it < pre; ++it)
-        tma_load_3d(smem + it * kStage + x_off(), &xmap, &full[it], 0, 0, (st_begin + it) * (kStageK / 16));
+        tma_load_3d(smem + it * C::kStage + C::kXOff, &xmap, &full[it], 0, 0, (st_begin + it) * (kStageK / 64));
       int issued = pre;
+      int slot = 0;            // slot of stage `it` (it >= S: slot = it % S)
+      uint32_t phase = 0;      // parity of the consumers' previous release of that slot
       for (int it = pre; it < n_it; ++it) {
-        const int slot = it % S;
-        if (!mbar_wait_bounded(&empty[slot], (uint32_t)(it / S - 1) & 1u, args.err, 1)) {
+        if (!mbar_wait_bounded(&empty[slot], phase, args.err, 1)) {
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
-        uint8_t* st = smem + slot * kStage;
+        uint8_t* st = smem + slot * C::kStage;
         const int stage = st_begin + it;
-        mbar_arrive_expect_tx(&full[slot], (uint32_t)stage_tx_bytes(NT));
+        mbar_arrive_expect_tx(&full[slot], args.tx_bytes);
         tma_load_2d_hint(st, &wmap, &full[slot], n0, stage * kWRows, pol);
-        tma_load_3d(st + x_off(), &xmap, &full[slot], 0, 0, stage * (kStageK / 16));
+        tma_load_3d(st + C::kXOff, &xmap, &full[slot], 0, 0, stage * (kStageK / 64));
         const int srow = (2 * stage) / args.rows_per_group;
-        tma_load_2d(st + s_off(NT), &smap, &full[slot], n0, srow);
-        tma_load_2d(st + z_off(NT), &zmap, &full[slot], n0, srow);
+        tma_load_2d(st + C::kSOff, &smap, &full[slot], n0, srow);
+        tma_load_2d(st + C::kZOff, &zmap, &full[slot], n0, srow);
         issued = it + 1;
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1u;
+        }
       }
       if (*abort_flag) {
         // drain: wait (bounded) for the copies this CTA still has in flight
@@ -293,78 +311,87 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const int pair = warp >> 1;
-    const int h = warp & 1;  // which group of the stage
-    for (int it = pair; it < n_it; it += kPairs) {
-      const int slot = it % S;
+    const int unit = warp % kUnits;
+    const int h = unit / (kCols / kCW);      // which group of the stage
+    const int cs = unit % (kCols / kCW);     // which 64-column half
+    const int cb = cs * kCW + g * kSpan;     // this thread's first column (byte) in the CTA tile
+    // x row a * 8 + g of 64-k chunk c sits at line c * M_pad + a * 8 + g, so its
+    // swizzle phase is g for every chunk and token tile
+    const bool one_row_groups = args.rows_per_group == 1;
+    int it = warp / kUnits;
+    int slot = it % S;           // ring slot and phase of stage `it`, advanced incrementally
+    uint32_t phase = (uint32_t)(it / S) & 1u;
+    for (; it < n_it; it += kStep) {
       if (*abort_flag) break;
-      if (!mbar_wait_bounded(&full[slot], (uint32_t)(it / S) & 1u, args.err, 2)) {
+      if (!mbar_wait_bounded(&full[slot], phase, args.err, 2)) {
         *abort_flag = 1;
         break;
       }
       const int stage = st_begin + it;
       const int chunk = 2 * stage + h;  // 128-k group-sized chunk index
       if (chunk < args.n_chunks) {
-        const uint8_t* st = smem + slot * kStage;
-        const int srow = chunk / args.rows_per_group - (2 * stage) / args.rows_per_group;
-        const PT* sv = reinterpret_cast<const PT*>(st + s_off(NT)) + srow * kCols + 16 * g;
-        const PT* zv = reinterpret_cast<const PT*>(st + z_off(NT)) + srow * kCols + 16 * g;
-        // per-column dequant constants for this thread's 16 columns, kept as
-        // pairs (columns 2j, 2j+1); the lane is selected where they are used
-        uint32_t sc2[8], zlo2[8], zhi2[8];
-        float sf[16], zf[16];
+        const uint8_t* st = smem + slot * C::kStage;
+        const uint8_t* xs = st + C::kXOff;
+        // per-column dequant constants of this thread's kSpan columns
+        const int prow = one_row_groups ? h : chunk / args.rows_per_group - (2 * stage) / args.rows_per_group;
+        const PT* sv = reinterpret_cast<const PT*>(st + C::kSOff) + prow * kCols + cb;
+        const PT* zv = reinterpret_cast<const PT*>(st + C::kZOff) + prow * kCols + cb;
+        uint32_t s2[kSpan], zlo[kSpan], zhi[kSpan];
+        float sf[kSpan], zf[kSpan];
         {
-          uint4 s4[2], z4[2];
-          s4[0] = reinterpret_cast<const uint4*>(sv)[0];
-          s4[1] = reinterpret_cast<const uint4*>(sv)[1];
-          z4[0] = reinterpret_cast<const uint4*>(zv)[0];
-          z4[1] = reinterpret_cast<const uint4*>(zv)[1];
-          if constexpr (kExact) {
-            const uint32_t* sw = reinterpret_cast<const uint32_t*>(s4);
-            const uint32_t* zw = reinterpret_cast<const uint32_t*>(z4);
+          const uint4 s4 = *reinterpret_cast<const uint4*>(sv);
+          const uint4 z4 = *reinterpret_cast<const uint4*>(zv);
+          if constexpr (kSameType) {
+            // splat each 16-bit value to both halves; (O + zero) is exact
+            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
+            const uint32_t olo = O::splat(O::kOffLo), ohi = O::splat(O::kOffHi);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              sc2[j] = sw[j];
-              zlo2[j] = O::add(zw[j], O::kOffLo2);  // exact: zeros are integers in [0, 15]
-              zhi2[j] = O::add(zw[j], O::kOffHi2);
+            for (int i = 0; i < kSpan; ++i) {
+              const uint32_t sel = (i & 1) ? 0x3232u : 0x1010u;
+              s2[i] = __byte_perm(sw[i >> 1], 0u, sel);
+              const uint32_t zz = __byte_perm(zw[i >> 1], 0u, sel);
+              zlo[i] = O::add(zz, olo);
+              zhi[i] = O::kOffLo == O::kOffHi ? zlo[i] : O::add(zz, ohi);
             }
           } else {
-            const PT* sp_ = reinterpret_cast<const PT*>(s4);
-            const PT* zp_ = reinterpret_cast<const PT*>(z4);
+            const PT* se = reinterpret_cast<const PT*>(&s4);
+            const PT* ze = reinterpret_cast<const PT*>(&z4);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              sf[i] = Num<PT>::to_f(sp_[i]);
-              zf[i] = Num<PT>::to_f(zp_[i]);
+            for (int i = 0; i < kSpan; ++i) {
+              sf[i] = Num<PT>::to_f(se[i]);
+              zf[i] = Num<PT>::to_f(ze[i]);
             }
           }
         }
-        const uint8_t* wbase = st + 64 * h * 128;                 // this group's 64 packed rows
-        const uint8_t* xbase = st + x_off() + 8 * h * kXChunk;    // this group's 8 x chunks
+        // packed rows 64 h + 8 s + 2 q (+1): swizzle phase 2 q (+1) for every s
+        const uint8_t* wr0 = st + (64 * h + 2 * q) * 128 + ((((cb >> 4) ^ (2 * q))) << 4) + (cb & 15);
+        const uint8_t* wr1 = st + (64 * h + 2 * q + 1) * 128 + ((((cb >> 4) ^ (2 * q + 1))) << 4) + (cb & 15);
+        const uint8_t* xr = xs + (2 * h * kMPad + g) * 128 + 8 * (q & 1);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const int r0 = 64 * h + 8 * s + 2 * q;  // row within the 128-row box (swizzle uses r & 7)
-          const int r1 = r0 + 1;
-          const uint4 wa = *reinterpret_cast<const uint4*>(wbase + (8 * s + 2 * q) * 128 + ((g ^ (r0 & 7)) << 4));
-          const uint4 wbv = *reinterpret_cast<const uint4*>(wbase + (8 * s + 2 * q + 1) * 128 + ((g ^ (r1 & 7)) << 4));
+          const uint2 wa = *reinterpret_cast<const uint2*>(wr0 + s * 1024);
+          const uint2 wb = *reinterpret_cast<const uint2*>(wr1 + s * 1024);
+          const uint32_t wav[2] = {wa.x, wa.y}, wbv[2] = {wb.x, wb.y};
+          // x[k .. k+3] for k = 128 h + 16 s + 4 q: 16-byte chunk 2 (s & 3) + q / 2 of
+          // line (2 h + s / 4) * M_pad + a * 8 + g
+          const int xoff = (s >> 2) * kMPad * 128 + ((((2 * (s & 3) + (q >> 1)) ^ g)) << 4);
           uint32_t b0[NT], b1[NT];
 #pragma unroll
           for (int a = 0; a < NT; ++a) {
-            const uint2 xv = *reinterpret_cast<const uint2*>(xbase + s * kXChunk + (a * 8 + g) * 32 + q * 8);
+            const uint2 xv = *reinterpret_cast<const uint2*>(xr + a * 8 * 128 + xoff);
             b0[a] = __byte_perm(xv.x, xv.y, 0x5410);  // (x[4q], x[4q+2])
             b1[a] = __byte_perm(xv.x, xv.y, 0x7632);  // (x[4q+1], x[4q+3])
           }
-          const uint32_t wa_w[4] = {wa.x, wa.y, wa.z, wa.w};
-          const uint32_t wb_w[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
+          for (int t = 0; t < kTiles; ++t) {
             uint32_t afr[4];
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               const int i = 2 * t + hh;
-              const uint32_t tt = __byte_perm(wa_w[i >> 2], wb_w[i >> 2], pair_sel(i & 3));
-              if constexpr (kExact) {
-                afr[hh] = O::mul_l(O::sub_l(O::lo(tt), zlo2[i >> 1], hh), sc2[i >> 1], hh);
-                afr[2 + hh] = O::mul_l(O::sub_l(O::hi(tt), zhi2[i >> 1], hh), sc2[i >> 1], hh);
+              const uint32_t tt = __byte_perm(wav[i >> 2], wbv[i >> 2], pair_sel(i & 3));
+              if constexpr (kSameType) {
+                afr[hh] = O::mul(O::sub(O::lo(tt), zlo[i]), s2[i]);      // k = 2 r0, 2 r0 + 2
+                afr[2 + hh] = O::mul(O::sub(O::hi(tt), zhi[i]), s2[i]);  // k = 2 r0 + 1, 2 r0 + 3
               } else {
                 const float a_lo = (float)(tt & 15u), a_hi = (float)((tt >> 4) & 15u);
                 const float b_lo = (float)((tt >> 16) & 15u), b_hi = (float)((tt >> 20) & 15u);
@@ -379,38 +406,48 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+      slot += kStep;
+      if (slot >= S) {
+        slot -= S;
+        phase ^= 1u;
+      }
     }
   }
 
   // ---------------------------------------------------------- reduction
   // The ring is free once every stage is consumed: reuse it as
-  // red[WK][M_pad][kRedPitch] (per warp) and cta[M_pad][kRedPitch].
+  // red[warp][M_pad][kRedPitch] and cta[M_pad][kRedPitch].
   float* red = reinterpret_cast<float*>(smem);
-  float* cta = red + (size_t)WK * kMPad * kRedPitch;
+  float* cta = red + (size_t)kWarps * kMPad * kRedPitch;
   const int rows = args.M < kMPad ? args.M : kMPad;
   const int tid = threadIdx.x;
-  if (warp < WK) {
+  if (warp < kWarps) {
     pdl_wait();  // output writes below must follow the previous kernel (PDL)
     named_barrier(1, kConsumers);
+    const int cb = (warp % kUnits % (kCols / kCW)) * kCW + g * kSpan;
 #pragma unroll
     for (int a = 0; a < NT; ++a) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = a * 8 + 2 * q + e;
+      for (int j = 0; j < 2; ++j) {
+        const int m = a * 8 + 2 * q + j;
         if (m < rows) {
-          float4* dst = reinterpret_cast<float4*>(red + ((size_t)warp * kMPad + m) * kRedPitch + 16 * g);
+          float4* dst = reinterpret_cast<float4*>(red + ((size_t)warp * kMPad + m) * kRedPitch + cb);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[j] = make_float4(acc[a][2 * j][e], acc[a][2 * j][2 + e], acc[a][2 * j + 1][e], acc[a][2 * j + 1][2 + e]);
+          for (int f = 0; f < kSpan / 4; ++f)
+            dst[f] = make_float4(acc[a][2 * f][j], acc[a][2 * f][2 + j], acc[a][2 * f + 1][j],
+                                 acc[a][2 * f + 1][2 + j]);
         }
       }
     }
     named_barrier(1, kConsumers);
     for (int idx = tid; idx < rows * (kCols / 4); idx += kConsumers) {
       const int m = idx / (kCols / 4), c4 = idx % (kCols / 4);
+      const int half = (4 * c4) / kCW;  // warps whose unit covers these columns
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int w = 0; w < WK; ++w) add4(v, reinterpret_cast<const float4*>(red + ((size_t)w * kMPad + m) * kRedPitch)[c4]);
+      for (int w = 0; w < kWarps; ++w)
+        if (w % kUnits % (kCols / kCW) == half)
+          add4(v, reinterpret_cast<const float4*>(red + ((size_t)w * kMPad + m) * kRedPitch)[c4]);
       if (args.ksplit == 1) {
         if (4 * c4 < valid_cols) finalize4<XT>(args, m, n0 + 4 * c4, v);
       } else {
@@ -423,7 +460,7 @@ __global__ void __launch_bounds__(32 * (warps_k(NT) + 1), ctas_per_sm(NT))
   // split-K across the cluster: rank r finalises columns [32r/ks, 32(r+1)/ks) (in float4s)
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
-  if (warp < WK) {
+  if (warp < kWarps) {
     const int ks = args.ksplit;
     const int r = (int)cluster.block_rank();
     const int c_lo = (kCols / 4) * r / ks, c_hi = (kCols / 4) * (r + 1) / ks;
@@ -447,32 +484,48 @@ struct Plan {
   size_t smem;
 };
 
+template <int NT>
+static void fill_ring(Plan& p) {
+  using C = Cfg<NT>;
+  const size_t budget = (size_t)(227 * 1024) - 2048;
+  // Ring slot i holds stages i, i+S, ... and is consumed by the same warps
+  // every time only if S is a multiple of the warps' stage stride; then a warp
+  // waits on the phases of its slots in order and an mbarrier parity wait can
+  // never alias a phase that belongs to other warps.
+  int S = (int)(budget / C::kStage);
+  if (S > 12) S = 12;
+  S = (S / kStep) * kStep;
+  if (S < kStep) S = kStep;
+  p.S = S;
+  size_t ring = (size_t)S * C::kStage;
+  if (ring < (size_t)C::kRed) ring = C::kRed;
+  p.smem = ring + 1024 + 2 * S * 8 + 64;
+}
+
 static Plan make_plan(int64_t M, int64_t N, int64_t K_pad) {
   Plan p{};
   p.nt = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
   p.n_stages = (int)cdiv(K_pad, kStageK);
-  const int sms = num_sms();
-  const int per_sm = ctas_per_sm(p.nt);
   p.n_cb = (int)cdiv(N, kCols);
-  const size_t budget = (size_t)(227 * 1024) / per_sm - 2048;
-  const size_t stage = (size_t)stage_bytes(p.nt);
-  // Ring slot i always holds stages i, i+S, ... of the same warp pair only if S
-  // is a multiple of the pair count: then a pair waits on the phases of its
-  // slots in order and an mbarrier parity wait can never alias a phase that
-  // belongs to the other pair.
-  int S = (int)(budget / stage);
-  if (S > 8) S = 8;
-  S = (S / kPairs) * kPairs;
-  if (S < kPairs) S = kPairs;
-  p.S = S;
-  size_t ring = (size_t)S * stage;
-  if (ring < (size_t)red_bytes(p.nt)) ring = red_bytes(p.nt);
-  p.smem = ring + 1024 + 2 * S * 8 + 64;
-  const int64_t target = (int64_t)per_sm * sms;
-  int64_t ks = (target + p.n_cb / 2) / p.n_cb;
-  if (ks > p.n_stages) ks = p.n_stages;
-  if (ks > kMaxCluster) ks = kMaxCluster;
-  if (ks < 1) ks = 1;
+  if (p.nt == 1) fill_ring<1>(p);
+  else if (p.nt == 2) fill_ring<2>(p);
+  else fill_ring<4>(p);
+  // Split K (a cluster of ks CTAs per column block). A CTA's time is about
+  // its stage count plus a fixed ramp (pipeline fill and the reduction, worth
+  // ~4 stages), and CTAs run in waves of one per SM: pick the split with the
+  // least waves x (stages per CTA + ramp), the smallest split on ties.
+  const int64_t slots = num_sms();
+  int64_t ks = 1;
+  int64_t best = -1;
+  for (int64_t k = 1; k <= kMaxCluster && k <= p.n_stages; ++k) {
+    const int64_t spc_k = cdiv(p.n_stages, k);
+    const int64_t ctas = p.n_cb * cdiv(p.n_stages, spc_k);
+    const int64_t cost = cdiv(ctas, slots) * (spc_k + 4);
+    if (best < 0 || cost < best) {
+      best = cost;
+      ks = k;
+    }
+  }
   const int64_t spc = cdiv(p.n_stages, ks);
   p.spc = (int)spc;
   p.ksplit = (int)cdiv(p.n_stages, spc);
@@ -486,7 +539,7 @@ bool gemv_supported(const QLinearProblem& pb) {
   if (!(pb.x_dtype == TF_F16 || pb.x_dtype == TF_BF16)) return false;
   if (!(pb.param_dtype == TF_F16 || pb.param_dtype == TF_BF16)) return false;
   if (pb.group_size % 128 != 0 || pb.K_pad % 128 != 0 || pb.K_pad == 0) return false;
-  if (pb.N % 16 != 0 || pb.ldx % 8 != 0 || pb.K % 16 != 0 || pb.K == 0) return false;
+  if (pb.N % 16 != 0 || pb.ldx % 8 != 0 || pb.K % 64 != 0 || pb.K == 0) return false;
   if (!aligned(pb.x, 16) || !aligned(pb.packed, 16) || !aligned(pb.scales, 16) || !aligned(pb.zeros, 16))
     return false;
   if (pb.N > 0x7fffffffLL || pb.K_pad / 2 > 0x7fffffffLL) return false;
@@ -506,7 +559,7 @@ static int launch_t(const gemv::Plan& p, const CUtensorMap* maps, const gemv::Ar
     attr_set[dev] = true;
   }
   return launch_ex("gemv_int4", kern, dim3((unsigned)p.n_cb, (unsigned)p.ksplit, 1),
-                   dim3(32 * (gemv::warps_k(NT) + 1), 1, 1), p.smem, st, dim3(1, (unsigned)p.ksplit, 1), maps[0],
+                   dim3(32 * (gemv::kWarps + 1), 1, 1), p.smem, st, dim3(1, (unsigned)p.ksplit, 1), maps[0],
                    maps[1], maps[2], maps[3], a);
 }
 
@@ -530,13 +583,14 @@ int gemv_launch(const QLinearProblem& pb, cudaStream_t st) {
                                 (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, gemv::kCols, gemv::kWRows,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  // x viewed as [K/16 chunks][M rows][16 k]: dims (16, M, K/16), strides (ldx*2, 32) bytes; box (16, M_pad, 16)
+  // x viewed as [K/64 chunks][M rows][64 k]: dims (64, M, K/64), strides (ldx*2, 128) bytes;
+  // box (64, M_pad, 4) = 4*M_pad lines of 128 B (rows >= M zero-filled), 128-byte swizzle
   {
-    const uint64_t dims[3] = {16, (uint64_t)pb.M, (uint64_t)(pb.K / 16)};
-    const uint64_t strides[2] = {(uint64_t)pb.ldx * 2, 32};
-    const uint32_t box[3] = {16, (uint32_t)(8 * p.nt), 16};
+    const uint64_t dims[3] = {64, (uint64_t)pb.M, (uint64_t)(pb.K / 64)};
+    const uint64_t strides[2] = {(uint64_t)pb.ldx * 2, 128};
+    const uint32_t box[3] = {64, (uint32_t)(8 * p.nt), 4};
     rc = encode_tensor_map_3d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_NONE);
+                              CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   const int64_t groups = pb.K_pad / pb.group_size;
@@ -560,6 +614,7 @@ int gemv_launch(const QLinearProblem& pb, cudaStream_t st) {
   a.ksplit = p.ksplit;
   a.rows_per_group = pb.group_size / 128;
   a.S = p.S;
+  a.tx_bytes = (uint32_t)(gemv::kWBoxBytes + 4 * 8 * p.nt * 128 + 2 * (2 * gemv::kCols * 2));
   const bool xh = pb.x_dtype == TF_F16, ph = pb.param_dtype == TF_F16;
   if (xh && ph) return launch_nt<__half, __half>(p, maps, a, st);
   if (!xh && !ph) return launch_nt<__nv_bfloat16, __nv_bfloat16>(p, maps, a, st);

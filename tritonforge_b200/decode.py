@@ -240,17 +240,33 @@ class QwenDecoder:
     `group` is a torch.distributed process group, or any object with an
     `all_reduce(tensor)` method that sums in place across the ranks."""
 
-    def __init__(self, model_or_weights, batch: int, max_len: int, group=None):
+    def __init__(self, model_or_weights, batch: int, max_len: int, group=None, vocab_parallel: bool | None = None):
         w = model_or_weights if isinstance(model_or_weights, QwenWeights) else QwenWeights.from_hf(model_or_weights)
         self.w = w
         self.model = w.model
         self.group = group
+        # Vocab-parallel lm_head (torch.distributed groups only): each rank
+        # scores its slice of the vocabulary and the ranks agree on the argmax
+        # through an all-gather of (best logit, token id) pairs.
+        self.world, self.rank = 1, 0
+        if group is not None and not hasattr(group, "all_reduce"):
+            import torch.distributed as dist
+
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.vocab_parallel = (self.world > 1) if vocab_parallel is None else (vocab_parallel and self.world > 1)
         self.B, self.T = batch, max_len
         self.H, self.I = w.hidden, w.inter
         self.Hq, self.Hkv, self.D = w.q_heads, w.kv_heads, w.head_dim
         self.eps = w.eps
         self.layers = w.layers
         self.final_norm, self.embed, self.lm_head = w.final_norm, w.embed, w.lm_head
+        self.vocab = w.lm_head.shape[0]
+        self.v0 = 0
+        if self.vocab_parallel:
+            from .tp import split_even
+
+            self.v0, v1 = split_even(self.vocab, self.world, self.rank)
+            self.lm_head = w.lm_head[self.v0:v1].contiguous()
         self.dev, self.dtype = w.device, w.dtype
         self.scale = self.D ** -0.5
         dev, dt, B = self.dev, self.dtype, batch
@@ -275,6 +291,10 @@ class QwenDecoder:
             "mlp": torch.empty(B, self.H, dtype=dt, device=dev),
             "logits": torch.empty(B, self.lm_head.shape[0], dtype=dt, device=dev),
         }
+        if self.vocab_parallel:
+            self.buf["best"] = torch.empty(B, 2, dtype=torch.float32, device=dev)     # (logit, token id)
+            self.buf["all_best"] = torch.empty(self.world, B, 2, dtype=torch.float32, device=dev)
+            self.buf["arg"] = torch.empty(B, dtype=torch.long, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self._lib = _lib.load()
         self._dt = _lib.dtype_code(dt)
@@ -332,9 +352,27 @@ class QwenDecoder:
             self._all_reduce(b["mlp"])
         kernels.rmsnorm_residual(b["mlp"], res, self.final_norm, self.eps, out=(b["normed"], res_next))
         torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
-        torch.argmax(b["logits"], dim=-1, out=self.tokens)
+        if self.vocab_parallel:
+            self._vocab_parallel_argmax()
+        else:
+            torch.argmax(b["logits"], dim=-1, out=self.tokens)
         self.pos.add_(1)
         return self.tokens
+
+    def _vocab_parallel_argmax(self) -> None:
+        """Greedy token over the whole vocabulary from each rank's slice of the
+        logits. Ties go to the smallest token id, as torch.argmax over the full
+        logits does (the first maximum): within a rank argmax takes the first,
+        across ranks the lowest rank (whose ids are smaller) wins."""
+        import torch.distributed as dist
+
+        from .tp import best_of_ranks, local_best
+
+        b = self.buf
+        local_best(b["logits"], self.v0, b["best"], b["arg"])
+        dist.all_gather_into_tensor(b["all_best"].view(-1, 2), b["best"], group=self.group)
+        tok = best_of_ranks(b["all_best"])
+        self.tokens.copy_(tok)
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step."""

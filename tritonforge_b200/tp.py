@@ -102,3 +102,22 @@ def synthetic_linear(n: int, k: int, gen: torch.Generator, device, dtype, std: f
     del w
     b = (torch.randn(n, generator=gen, device=device) * std).to(dtype) if bias else None
     return QuantLinear(packed, scales, zeros, k, n, b, GROUP)
+
+
+def local_best(logits: torch.Tensor, v0: int, out: torch.Tensor, arg: torch.Tensor) -> torch.Tensor:
+    """(best logit, global token id) per row of this rank's vocabulary slice
+    `logits` [B, V_local] (ids offset by v0), as fp32 pairs in `out` [B, 2];
+    the first maximum within the slice wins, as in torch.argmax."""
+    torch.argmax(logits, dim=-1, out=arg)
+    out[:, :1].copy_(torch.gather(logits, 1, arg.unsqueeze(1)))  # exact: fp16/bf16 values fit in fp32
+    out[:, 1].copy_(arg).add_(v0)                               # exact: ids < 2^24
+    return out
+
+
+def best_of_ranks(all_best: torch.Tensor) -> torch.Tensor:
+    """Token ids [B] (fp32) from every rank's (best logit, id) pairs
+    [world, B, 2], ranks holding consecutive vocabulary slices in rank order:
+    the largest logit wins and ties go to the lowest rank, whose ids are the
+    smallest, so the result equals torch.argmax over the whole vocabulary."""
+    win = torch.argmax(all_best[:, :, 0], dim=0)
+    return torch.gather(all_best[:, :, 1], 0, win.unsqueeze(0)).squeeze(0)
