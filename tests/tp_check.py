@@ -63,16 +63,22 @@ def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
     dst.pos.copy_(src.pos)
 
 
-def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> tuple[bool, float, float]:
-    """max |got - ref| <= tol x RMS(ref), after allowing each element one ulp
-    of its own bf16 rounding (row-parallel partial sums are rounded to bf16
-    before the all-reduce adds them, so a logit of magnitude 8 may differ by
-    its ulp, 0.0625, which is 5% of an RMS near 1.2)."""
+def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2, ulps: int = 4) -> tuple[bool, float, float]:
+    """Tensor-parallel logits against tp=1 logits of the same weights.
+
+    Row-parallel partial sums are rounded to bf16 before the all-reduce adds
+    them (one extra rounding of the residual stream per row-parallel layer),
+    so logits may differ by a few bf16 ulps of their own magnitude: a logit
+    near 10 has an ulp of 0.0625, 5% of an RMS near 1.2. The check is
+    max(|got - ref| - ulps x ulp(ref)) <= tol x RMS(ref), and the mean
+    |got - ref| <= tol / 4 x RMS(ref)."""
     ref32 = ref.float()
     ulp = torch.ldexp(torch.ones_like(ref32), torch.frexp(ref32)[1] - 8)  # bf16 ulp of each value
-    err = float(((got.float() - ref32).abs() - ulp).clamp_min(0).max())
+    diff = (got.float() - ref32).abs()
+    err = float((diff - ulps * ulp).clamp_min(0).max())
     rms = float(ref32.pow(2).mean().sqrt())
-    return err <= tol * rms, err, rms
+    mean = float(diff.mean())
+    return err <= tol * rms and mean <= tol / 4 * rms, err, rms
 
 
 def _nccl_main() -> int:

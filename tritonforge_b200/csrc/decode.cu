@@ -62,23 +62,78 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, int64_t ld_qkv, T*
   }
 }
 
-// Decode attention (flash-decoding): the cached positions of one (batch row,
-// kv head) are split into `splits` chunks, one CTA each; the CTAs of a
-// (row, head) form a thread-block cluster. A CTA handles the G = hq/hkv q heads
-// of its kv head over its chunk:
-//   scores  s[g, t] = (q_g . k_t) * scale       threads over positions
-//   softmax m_g = max_t s, p = exp(s - m_g), l_g = sum_t p
-//   output  o[g, :] = sum_t p[g, t] v_t          warps over positions, lanes over D
-// and the chunks are combined through distributed shared memory:
-//   M = max_c m_c, L = sum_c l_c e^(m_c - M), O = sum_c o_c e^(m_c - M) / L.
-// All in fp32; the output is rounded once to the model dtype.
+// Decode attention (flash-decoding on the tensor pipe): the cached positions
+// of one (batch row, kv head) are split into `splits` chunks, one CTA each;
+// the CTAs of a (row, head) form a thread-block cluster. Within a CTA the 4
+// warps take 16-position tiles of the chunk in turn; per tile a warp computes
+//   S = Q K^T        mma.sync m16n8k16: A = the G (<= 8) q heads of this kv
+//                    head (rows G..15 zero), B = K^T; d is permuted the same
+//                    way for Q and K so a thread's K fragment is 32 (D=128) or
+//                    16 (D=64) consecutive elements of one cached row, loaded
+//                    with 16-byte global loads
+//   online softmax   running max m and sum l per head in fp32 (scale applied
+//                    to the fp32 scores; positions past the length masked)
+//   O += P V         A = P rounded to the model dtype, B = V staged in shared
+//                    memory by cp.async and read with ldmatrix.trans
+// The warps' (m, l, O) are merged in shared memory and the chunks of the
+// cluster through distributed shared memory:
+//   M = max_c m_c, L = sum_c l_c e^(m_c - M), O = sum_c o_c e^(m_c - M) / L,
+// all in fp32; the output is rounded once to the model dtype.
+template <typename T> struct AttnMma;
+template <> struct AttnMma<__half> {
+  static __device__ __forceinline__ void mma(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+template <> struct AttnMma<__nv_bfloat16> {
+  static __device__ __forceinline__ void mma(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
                                                           const T* __restrict__ v_cache, T* __restrict__ out,
                                                           const int* __restrict__ len_ptr, int hq, int hkv,
                                                           int t_max, int chunk, float scale) {
-  constexpr int kThreads = 128, kWarps = 4, kPerLane = D / 32;
-  extern __shared__ float sm[];
+  constexpr int kWarps = 4, kThreads = 32 * kWarps;
+  constexpr int kSteps = D / 16;       // k-steps of S = Q K^T
+  constexpr int kWords = D / 8;        // 32-bit words of a thread's K / Q slice (D/4 elements)
+  constexpr int kNT = D / 8;           // n-tiles (8 dims) of O
+  constexpr int kChunks = D / 8;       // 16-byte chunks of a cached row
+  constexpr int kVTile = 16 * D * 2;   // bytes of one staged V tile
+  using MM = AttnMma<T>;
+  extern __shared__ __align__(16) uint8_t attn_smem[];
   pdl_trigger();
   pdl_wait();
   const int kh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, splits = gridDim.z;
@@ -89,94 +144,174 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ 
   int t_end = t_begin + chunk;
   if (t_end > len) t_end = len;
   const int n = t_end > t_begin ? t_end - t_begin : 0;
-  float* qf = sm;                                 // [G][D]
-  float* p = qf + g_count * D;                    // [G][chunk]
-  float* o_part = p + (size_t)g_count * chunk;    // [kWarps][G][D]
-  float* stats = o_part + kWarps * g_count * D;   // [G] max, [G] sum
-  float* o_cta = stats + 2 * g_count;             // [G][D] (this CTA's unnormalised output)
+  const int n_tiles = (n + 15) / 16;
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const T* qb = q + ((int64_t)b * hq + (int64_t)kh * g_count) * D;
-  for (int i = tid; i < g_count * D; i += kThreads) qf[i] = Num<T>::to_f(qb[i]);
-  __syncthreads();
+  const int g = lane >> 2, qd = lane & 3;
+  uint8_t* vbuf = attn_smem + warp * 2 * kVTile;                        // [2][16 rows][D] per warp, swizzled
+  float* m_w = reinterpret_cast<float*>(attn_smem + kWarps * 2 * kVTile);  // [kWarps][8]
+  float* l_w = m_w + kWarps * 8;                                          // [kWarps][8]
+  float* o_w = l_w + kWarps * 8;                                          // [kWarps][8][D]
+  float* stats = o_w + kWarps * 8 * D;                                    // [G] max, [G] sum (CTA)
+  float* o_cta = stats + 16;                                              // [G][D] (unnormalised)
+
   const T* kb = k_cache + ((int64_t)b * hkv + kh) * t_max * D;
   const T* vb = v_cache + ((int64_t)b * hkv + kh) * t_max * D;
-  // scores: each thread owns positions t_begin + tid, + kThreads, ...
-  for (int j = tid; j < n; j += kThreads) {
-    const int t = t_begin + j;
-    float kv[D];
-    const uint4* k4 = reinterpret_cast<const uint4*>(kb + (int64_t)t * D);
+  // Q fragment: head g of this kv head, elements [qd*D/4, (qd+1)*D/4)
+  uint32_t qf[kWords];
+  if (g < g_count) {
+    const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)b * hq + (int64_t)kh * g_count + g) * D + qd * (D / 4));
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 raw = __ldg(k4 + c);
-      const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) kv[8 * c + u] = Num<T>::to_f(e[u]);
+    for (int c = 0; c < kWords / 4; ++c) {
+      const uint4 v = __ldg(qs + c);
+      qf[4 * c] = v.x; qf[4 * c + 1] = v.y; qf[4 * c + 2] = v.z; qf[4 * c + 3] = v.w;
     }
-    for (int g = 0; g < g_count; ++g) {
-      float acc = 0.f;
+  } else {
 #pragma unroll
-      for (int d = 0; d < D; ++d) acc = fmaf(qf[g * D + d], kv[d], acc);
-      p[(size_t)g * chunk + j] = acc * scale;
-    }
+    for (int c = 0; c < kWords; ++c) qf[c] = 0u;
   }
-  __syncthreads();
-  // chunk softmax statistics: warp w handles heads w, w + 4, ...
-  for (int g = warp; g < g_count; g += kWarps) {
-    float mx = -INFINITY;
-    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, p[(size_t)g * chunk + j]);
+
+  float o_acc[kNT][4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = expf(p[(size_t)g * chunk + j] - mx);
-      p[(size_t)g * chunk + j] = e;
-      sum += e;
-    }
+  for (int j = 0; j < kNT; ++j)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) {
-      stats[g] = mx;
-      stats[g_count + g] = sum;
-    }
-  }
-  __syncthreads();
-  // p . v: warp w takes positions j = w, w + 4, ...; lane owns D/32 consecutive dims
-  float acc[8][kPerLane];
+    for (int e = 0; e < 4; ++e) o_acc[j][e] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // of head g (same in the 4 threads of a group)
+
+  // K fragments of a 16-position tile: n-tile h in {0,1}, position t0 + 8h + g
+  auto load_k = [&](int tile, uint32_t (*kf)[kWords]) {
 #pragma unroll
-  for (int g = 0; g < 8; ++g)
+    for (int h = 0; h < 2; ++h) {
+      int t = t_begin + tile * 16 + 8 * h + g;
+      t = t < t_end ? t : (t_end > 0 ? t_end - 1 : 0);
+      const uint4* ks = reinterpret_cast<const uint4*>(kb + (int64_t)t * D + qd * (D / 4));
 #pragma unroll
-    for (int e = 0; e < kPerLane; ++e) acc[g][e] = 0.f;
-  for (int j = warp; j < n; j += kWarps) {
-    const T* vrow = vb + (int64_t)(t_begin + j) * D + lane * kPerLane;
-    float vv[kPerLane];
-#pragma unroll
-    for (int e = 0; e < kPerLane; ++e) vv[e] = Num<T>::to_f(vrow[e]);
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      if (g < g_count) {
-        const float pg = p[(size_t)g * chunk + j];
-#pragma unroll
-        for (int e = 0; e < kPerLane; ++e) acc[g][e] = fmaf(pg, vv[e], acc[g][e]);
+      for (int c = 0; c < kWords / 4; ++c) {
+        const uint4 v = __ldg(ks + c);
+        kf[h][4 * c] = v.x; kf[h][4 * c + 1] = v.y; kf[h][4 * c + 2] = v.z; kf[h][4 * c + 3] = v.w;
       }
     }
+  };
+  // V tile -> shared memory (16-byte chunk c of row r at chunk c ^ (r & 7)); rows past the end are zero
+  auto stage_v = [&](int tile, int buf) {
+    const uint32_t base = smem_u32(vbuf + buf * kVTile);
+#pragma unroll
+    for (int i = lane; i < 16 * kChunks; i += 32) {
+      const int r = i / kChunks, c = i % kChunks;
+      const int t = t_begin + tile * 16 + r;
+      const bool ok = t < t_end;
+      const T* src = vb + (int64_t)(ok ? t : 0) * D + c * 8;
+      cp_async16(base + r * (D * 2) + ((c ^ (r & 7)) << 4), src, ok ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+
+  uint32_t kf[2][kWords];
+  int tile = warp;
+  if (tile < n_tiles) {
+    load_k(tile, kf);
+    stage_v(tile, 0);
   }
+  for (int it = 0; tile < n_tiles; ++it, tile += kWarps) {
+    const int buf = it & 1;
+    const int next = tile + kWarps;
+    if (next < n_tiles) stage_v(next, buf ^ 1);
+    // S = Q K^T for the 16 positions of the tile (two n-tiles of 8)
+    float sc[2][4];
 #pragma unroll
-  for (int g = 0; g < 8; ++g)
-    if (g < g_count)
+    for (int h = 0; h < 2; ++h) {
 #pragma unroll
-      for (int e = 0; e < kPerLane; ++e) o_part[((size_t)warp * g_count + g) * D + lane * kPerLane + e] = acc[g][e];
+      for (int e = 0; e < 4; ++e) sc[h][e] = 0.f;
+#pragma unroll
+      for (int s = 0; s < kSteps; ++s) MM::mma(sc[h], qf[2 * s], qf[2 * s + 1], kf[h][2 * s], kf[h][2 * s + 1]);
+    }
+    if (next < n_tiles) load_k(next, kf);  // in flight during the softmax and P.V below
+    // online softmax over head g's 16 scores (this thread: positions 2qd, 2qd+1 of each n-tile)
+    float sv[4];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = t_begin + tile * 16 + 8 * h + 2 * qd + e;
+        const float v = t < t_end ? sc[h][e] * scale : -INFINITY;
+        sv[2 * h + e] = v;
+        mt = fmaxf(mt, v);
+      }
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+    const float m_new = fmaxf(m_run, mt);  // finite: every tile holds at least one valid position
+    const float corr = expf(m_run - m_new);
+    float ps[4], lt = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ps[i] = expf(sv[i] - m_new);
+      lt += ps[i];
+    }
+    lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+    l_run = l_run * corr + lt;
+    m_run = m_new;
+#pragma unroll
+    for (int j = 0; j < kNT; ++j) {
+      o_acc[j][0] *= corr;
+      o_acc[j][1] *= corr;
+    }
+    const uint32_t pa0 = MM::pack(ps[0], ps[1]), pa2 = MM::pack(ps[2], ps[3]);
+    // O += P V
+    if (next < n_tiles) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncwarp();
+    const uint32_t vbase = smem_u32(vbuf + buf * kVTile);
+#pragma unroll
+    for (int dc = 0; dc < D / 16; ++dc) {
+      // matrix mi = lane >> 3: rows (positions) 8 (mi & 1) + (lane & 7), dims 16 dc + 8 (mi >> 1)
+      const int r = 8 * ((lane >> 3) & 1) + (lane & 7);
+      const int c = 2 * dc + (lane >> 4);
+      uint32_t vf[4];
+      ldsm_x4_trans(vbase + r * (D * 2) + ((c ^ (r & 7)) << 4), vf);
+      MM::mma(o_acc[2 * dc], pa0, pa2, vf[0], vf[1]);
+      MM::mma(o_acc[2 * dc + 1], pa0, pa2, vf[2], vf[3]);
+    }
+    __syncwarp();  // the buffer is refilled two tiles later
+  }
+
+  // merge the warps: (m, l) per head, O rows g (columns 2qd, 2qd+1 of each n-tile)
+  if (qd == 0 && g < 8) {
+    m_w[warp * 8 + g] = m_run;
+    l_w[warp * 8 + g] = l_run;
+  }
+  if (g < g_count) {
+#pragma unroll
+    for (int j = 0; j < kNT; ++j) {
+      o_w[(warp * 8 + g) * D + 8 * j + 2 * qd] = o_acc[j][0];
+      o_w[(warp * 8 + g) * D + 8 * j + 2 * qd + 1] = o_acc[j][1];
+    }
+  }
   __syncthreads();
-  for (int i = tid; i < g_count * D; i += kThreads) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += o_part[(size_t)w * g_count * D + i];
-    o_cta[i] = s;
+  if (tid < g_count) {
+    float mx = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, m_w[w * 8 + tid]);
+    float l = 0.f;
+    for (int w = 0; w < kWarps; ++w)
+      if (l_w[w * 8 + tid] > 0.f) l += l_w[w * 8 + tid] * expf(m_w[w * 8 + tid] - mx);
+    stats[tid] = mx;
+    stats[8 + tid] = l;
   }
+  for (int i = tid; i < g_count * D; i += kThreads) {
+    const int gg = i / D;
+    float mx = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, m_w[w * 8 + gg]);
+    float o = 0.f;
+    for (int w = 0; w < kWarps; ++w)
+      if (l_w[w * 8 + gg] > 0.f) o += o_w[(w * 8 + gg) * D + i % D] * expf(m_w[w * 8 + gg] - mx);
+    o_cta[i] = o;
+  }
+  __syncthreads();
   T* ob = out + ((int64_t)b * hq + (int64_t)kh * g_count) * D;
   if (splits == 1) {
-    __syncthreads();
     for (int i = tid; i < g_count * D; i += kThreads) {
-      const float l = stats[g_count + i / D];
+      const float l = stats[8 + i / D];
       ob[i] = Num<T>::from_f(l > 0.f ? o_cta[i] / l : 0.f);
     }
     return;
@@ -188,18 +323,18 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ 
   const int items = g_count * D;
   const int lo = items * r / splits, hi = items * (r + 1) / splits;
   for (int i = lo + tid; i < hi; i += kThreads) {
-    const int g = i / D;
+    const int gg = i / D;
     float mx = -INFINITY;
     for (int c = 0; c < splits; ++c) {
       const float* st = cluster.map_shared_rank(stats, c);
-      if (st[g_count + g] > 0.f) mx = fmaxf(mx, st[g]);
+      if (st[8 + gg] > 0.f) mx = fmaxf(mx, st[gg]);
     }
     float l = 0.f, o = 0.f;
     for (int c = 0; c < splits; ++c) {
       const float* st = cluster.map_shared_rank(stats, c);
-      const float lc = st[g_count + g];
+      const float lc = st[8 + gg];
       if (lc > 0.f) {
-        const float w = expf(st[g] - mx);
+        const float w = expf(st[gg] - mx);
         l += lc * w;
         o += cluster.map_shared_rank(o_cta, c)[i] * w;
       }
@@ -255,9 +390,9 @@ extern "C" int tf_rope_kv_append(const void* qkv, int64_t ld_qkv, void* q_out, c
 
 namespace tf {
 namespace {
-size_t decode_attention_smem(int g, int head_dim, int chunk) {
-  return ((size_t)g * head_dim + (size_t)g * chunk + 4 * (size_t)g * head_dim + 2 * g + (size_t)g * head_dim) *
-         sizeof(float);
+size_t decode_attention_smem(int head_dim) {
+  // V tiles [4 warps][2][16][D] (model dtype) + per-warp (m, l, O[8][D]) + CTA stats and O[8][D]
+  return (size_t)4 * 2 * 16 * head_dim * 2 + (4 * 8 * 2 + 4 * 8 * (size_t)head_dim + 16 + 8 * (size_t)head_dim) * 4;
 }
 }  // namespace
 }  // namespace tf
@@ -274,16 +409,19 @@ extern "C" int tf_decode_attention(const void* q, const void* k_cache, const voi
   if (B > 65535) return fail(TF_ERR_BAD_SHAPE, "decode_attention: batch too large");
   if (!q || !k_cache || !v_cache || !out || !len) return fail(TF_ERR_BAD_ARG, "decode_attention: null pointer");
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(TF_ERR_UNALIGNED, "decode_attention: caches must be 16-byte aligned");
-  // split the context over a cluster so that there are >= 2 CTAs per SM when the batch is small
+  // split the context over a cluster: >= 2 CTAs per SM when the batch is
+  // small, and chunks of at most 512 positions (up to 8 splits) so that long
+  // contexts keep several CTAs resident per SM
   const int64_t rows = B * hkv;
   int splits = (int)cdiv(2LL * num_sms(), rows);
+  const int by_chunk = (int)cdiv(t_max, 512);
+  if (splits < by_chunk) splits = by_chunk;
   const int max_by_len = (int)cdiv(t_max, 64);
   if (splits > max_by_len) splits = max_by_len;
   if (splits > 8) splits = 8;
   if (splits < 1) splits = 1;
   const int chunk = (int)cdiv(t_max, splits);
-  const size_t smem = decode_attention_smem(g, head_dim, chunk);
-  if (smem > 227 * 1024) return fail(TF_ERR_UNSUPPORTED, "decode_attention: context too long (%zu B of shared memory)", smem);
+  const size_t smem = decode_attention_smem(head_dim);
   const dim3 grid((unsigned)hkv, (unsigned)B, (unsigned)splits), cluster(1, 1, (unsigned)splits);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TF_ATTN(T, DD)                                                                                          \
