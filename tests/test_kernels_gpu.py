@@ -248,3 +248,17 @@ def test_quantize_cpu_input_round_trip_device():
     recon = quant.quantize_dequantize(w.cuda(), group_size=128)
     err = quant.quantization_error(w.cuda(), recon)
     assert err["max_abs"] < 0.3 and err["mean_abs"] < 0.12  # reference tests/test_quant.py:30-36
+
+
+# ---- prefill regime (tcgen05 GEMM) -----------------------------------------
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", [(33, 128, 128), (64, 256, 896), (128, 128, 1024), (200, 384, 512),
+                                   (512, 640, 640), (600, 144, 1152), (1100, 4864, 896)])
+def test_gemm_regime(m, n, k, dtype):
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, seed=m + k)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemm"})
+    rows = torch.arange(m) if m <= 256 else torch.randperm(m, generator=torch.Generator().manual_seed(1))[:96].sort().values
+    ref = oracle_linear(x[rows.cuda()], packed, scales, zeros, b)
+    assert_rms_close(out[rows.cuda()], ref, dtype, f"gemm {m}x{n}x{k}")
+    again = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemm"})
+    assert torch.equal(out, again), "deterministic"

@@ -1,7 +1,7 @@
 """GPU tests of tensor-parallel decode: shards of the same int4 weights,
 decoded as TP ranks (threads on one GPU, or NCCL ranks on several GPUs),
-match a tp=1 decode of the full weights within the bf16 tolerance (2e-2 x RMS
-of the logits), and the ranks agree bit for bit."""
+match a tp=1 decode of the full weights within bf16 rounding noise (see
+tests.tp_check.logits_close), and the ranks agree bit for bit."""
 
 from __future__ import annotations
 
@@ -56,7 +56,7 @@ def test_tp_threads_match_tp1(name, tp, layers):
         for d in decs[1:]:
             assert torch.equal(d.buf["logits"], decs[0].buf["logits"])
         ok, err, rms = logits_close(decs[0].buf["logits"], ref.buf["logits"])
-        assert ok, f"tp{tp} logits max-abs {err:.4g} > 2e-2 x RMS {rms:.4g}"
+        assert ok, f"tp{tp} logits: max-abs beyond 4 ulps {err:.4g} (tolerance 6e-2 x RMS {rms:.4g})"
         for d in decs:
             d.tokens.copy_(ref.tokens)
 

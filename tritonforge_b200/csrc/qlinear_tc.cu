@@ -1,13 +1,411 @@
-// Prefill-regime int4 linear on the 5th-generation tensor cores (placeholder
-// until the tcgen05 kernel lands: reports the regime as unavailable).
+// Prefill-regime int4 linear on the 5th-generation tensor cores (tcgen05 with
+// TMEM accumulators): out[M, N] = x[M, K] @ W[K, N] (+ bias), for M > 32.
+//
+// Replaces the reference's large-M path, which either re-dequantises the
+// weight tile for every row tile (src/tritonforge/kernels/dequant_gemm.py:39-113)
+// or dequantises the whole weight and calls cuBLAS (integration/qwen.py:91-97).
+// Here each CTA owns 128 output columns and a group of up to 512 rows
+// (4 row tiles of 128) and walks K in chunks of 64:
+//  * a TMA warp loads, per chunk, the x tiles of the row tiles ([128 rows x
+//    64 k], 128-byte swizzle: the K-major UMMA canonical layout), the packed
+//    weights [32 packed rows x 128 columns] and the chunk's scale/zero rows;
+//  * 4 dequantisation warps turn the packed chunk into a [64 k x 128 n] tile
+//    of the activation type in shared memory, once for all row tiles, in the
+//    MN-major 128-byte-swizzled UMMA layout, with the reference's rounding:
+//    w = round_x((code - zero) * scale) (quant.py:90-105, reference.py:21-35).
+//    A nibble becomes (O + code) with one lop3 against a magic exponent, the
+//    subtraction of (O + zero) is exact and the multiply by the scale rounds
+//    once, so every weight equals the oracle's bit for bit;
+//  * one thread issues tcgen05.mma (kind::f16, M=128, N=128, K=16, fp32
+//    accumulators in TMEM: 4 row tiles x 128 columns = all 512 columns) and
+//    commits each chunk to an mbarrier that frees its ring slot;
+//  * the 4 dequantisation warps then read the accumulators back with
+//    tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = rows), round to the
+//    activation type, add the bias and round again (reference.py:33-35).
+// Every mbarrier wait is bounded (1 s): on expiry the kernel records an error
+// bit in the workspace header, stops issuing work, waits (bounded) for what is
+// in flight, frees its TMEM and finishes.
+#include "common.cuh"
 #include "qlinear.cuh"
 
 namespace tf {
+namespace tc {
 
-bool gemm_supported(const QLinearProblem&) { return false; }
+constexpr int kN = 128;            // output columns per CTA (UMMA N)
+constexpr int kMT = 128;           // rows per row tile (UMMA M)
+constexpr int kMaxTiles = 4;       // row tiles per CTA: 4 x 128 TMEM columns
+constexpr int kKC = 64;            // k per chunk (one 128-byte swizzle atom of halves)
+constexpr int kStages = 2;
+constexpr int kDeqWarps = 4;
+constexpr int kThreads = 32 * (kDeqWarps + 2);  // + TMA warp + MMA warp
+
+// stage layout (bytes; the UMMA operand tiles are 1024-byte aligned)
+constexpr int kXTile = kMT * kKC * 2;           // 16 KiB per row tile
+constexpr int kXOff = 0;
+constexpr int kBOff = kMaxTiles * kXTile;       // dequantised [64 k][128 n]: 2 atoms of 64 n x 64 k rows
+constexpr int kBBytes = kKC * kN * 2;           // 16 KiB
+constexpr int kWOff = kBOff + kBBytes;          // packed [32 rows][128 B]
+constexpr int kWBytes = (kKC / 2) * kN;         // 4 KiB
+constexpr int kSOff = kWOff + kWBytes;
+constexpr int kZOff = kSOff + kN * 2;
+constexpr int kStage = ((kZOff + kN * 2) + 1023) / 1024 * 1024;
+
+struct Args {
+  const void* bias;
+  void* out;
+  int* err;
+  int64_t ldo;
+  int M, N;
+  int n_chunks;        // K / 64
+  int group_size;
+  int bias_dtype;
+  uint32_t idesc;      // tcgen05 instruction descriptor
+};
+
+template <typename T> struct Deq;
+template <> struct Deq<__half> {
+  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, 0x64006400u); }
+  static __device__ __forceinline__ uint32_t hi(uint32_t t) { return lop3_and_or(t, 0x00F000F0u, 0x54005400u); }
+  static __device__ __forceinline__ uint32_t off_lo() { return 0x64006400u; }  // (1024, 1024)
+  static __device__ __forceinline__ uint32_t off_hi() { return 0x54005400u; }  // (64, 64)
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+};
+template <> struct Deq<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t lo(uint32_t t) { return lop3_and_or(t, 0x000F000Fu, 0x43004300u); }
+  static __device__ __forceinline__ uint32_t hi(uint32_t t) {
+    return lop3_and_or(__umulhi(t, 0x10000000u), 0x000F000Fu, 0x43004300u);  // t >> 4 on the FMA pipe
+  }
+  static __device__ __forceinline__ uint32_t off_lo() { return 0x43004300u; }  // (128, 128)
+  static __device__ __forceinline__ uint32_t off_hi() { return 0x43004300u; }
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+};
+
+// UMMA shared-memory descriptor: start, leading / stride byte offsets (all
+// >> 4), version 1 (bits 46-47), 128-byte swizzle (layout type 2, bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <typename XT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                        const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
+                        const Args args) {
+  using D = Deq<XT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);  // TMA bytes landed
+  uint64_t* bready = full + kStages;                                      // dequantised tile written
+  uint64_t* freed = bready + kStages;                                     // MMAs of the slot done
+  uint64_t* accum = freed + kStages;                                      // all MMAs done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kN;
+  const int m0 = blockIdx.y * kMT * kMaxTiles;
+  int tiles = (args.M - m0 + kMT - 1) / kMT;
+  if (tiles > kMaxTiles) tiles = kMaxTiles;
+  const int n_chunks = args.n_chunks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&bready[i], kDeqWarps);
+      mbar_init(&freed[i], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0) {
+    // all 512 TMEM columns: 4 row tiles x 128 fp32 accumulator columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == kDeqWarps) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      prefetch_tensormap(&xmap);
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&smap);
+      prefetch_tensormap(&zmap);
+      pdl_wait();
+      const uint32_t tx = (uint32_t)(tiles * kXTile + kWBytes + 2 * kN * 2);
+      int issued = 0;
+      for (int c = 0; c < n_chunks; ++c) {
+        const int slot = c % kStages;
+        if (c >= kStages && !mbar_wait_bounded(&freed[slot], (uint32_t)(c / kStages - 1) & 1u, args.err, 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        uint8_t* st = smem + slot * kStage;
+        mbar_arrive_expect_tx(&full[slot], tx);
+        for (int t = 0; t < tiles; ++t) tma_load_2d(st + kXOff + t * kXTile, &xmap, &full[slot], c * kKC, m0 + t * kMT);
+        tma_load_2d(st + kWOff, &wmap, &full[slot], n0, c * (kKC / 2));
+        const int grow = (c * kKC) / args.group_size;
+        tma_load_2d(st + kSOff, &smap, &full[slot], n0, grow);
+        tma_load_2d(st + kZOff, &zmap, &full[slot], n0, grow);
+        issued = c + 1;
+      }
+      if (*abort_flag) {
+        for (int c = (issued > kStages ? issued - kStages : 0); c < issued; ++c)
+          mbar_wait_bounded(&full[c % kStages], (uint32_t)(c / kStages) & 1u, args.err, 4);
+      }
+    }
+  } else if (warp == kDeqWarps + 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      for (int c = 0; c < n_chunks; ++c) {
+        const int slot = c % kStages;
+        const uint32_t ph = (uint32_t)(c / kStages) & 1u;
+        if (*abort_flag) break;
+        if (!mbar_wait_bounded(&full[slot], ph, args.err, 2) || !mbar_wait_bounded(&bready[slot], ph, args.err, 2)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + slot * kStage);
+#pragma unroll
+        for (int ks = 0; ks < kKC / 16; ++ks) {
+          // B: MN-major, atoms of 64 n x 8 k rows (1 KiB); next 8 k rows +1 KiB (SBO),
+          // next 64 n +8 KiB (LBO); a 16-k step starts 2 KiB further
+          const uint64_t bdesc = umma_desc(st + kBOff + ks * 2048, 8192, 1024);
+          for (int t = 0; t < tiles; ++t) {
+            // A: K-major rows of 128 B, 8-row atoms 1 KiB apart (SBO); a 16-k step is 32 B
+            const uint64_t adesc = umma_desc(st + kXOff + t * kXTile + ks * 32, 16, 1024);
+            umma_f16(tmem + t * kN, adesc, bdesc, args.idesc, (c > 0 || ks > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&freed[slot]);
+      }
+      umma_commit(accum);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    // ------------------------------------------------------ dequantisation
+    const int tid = threadIdx.x;  // 0..127
+    for (int c = 0; c < n_chunks; ++c) {
+      const int slot = c % kStages;
+      if (*abort_flag) break;
+      if (!mbar_wait_bounded(&full[slot], (uint32_t)(c / kStages) & 1u, args.err, 2)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* st = smem + slot * kStage;
+      const XT* sv = reinterpret_cast<const XT*>(st + kSOff);
+      const XT* zv = reinterpret_cast<const XT*>(st + kZOff);
+#pragma unroll
+      for (int item = 0; item < 4; ++item) {
+        const int i = tid + 128 * item;
+        const int j = i >> 4;         // packed row: k = 2j, 2j + 1 of the chunk
+        const int cg = i & 15;        // columns 8 cg .. 8 cg + 7
+        const uint2 pw = *reinterpret_cast<const uint2*>(st + kWOff + j * kN + 8 * cg);
+        const uint4 s4 = *reinterpret_cast<const uint4*>(sv + 8 * cg);
+        const uint4 z4 = *reinterpret_cast<const uint4*>(zv + 8 * cg);
+        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          // bytes of columns 8cg + 2p, 8cg + 2p + 1 into byte lanes 0 and 2
+          const uint32_t word = p < 2 ? pw.x : pw.y;
+          const uint32_t tt = __byte_perm(word, 0u, (p & 1) ? 0x4342u : 0x4140u);
+          lo[p] = D::mul(D::sub(D::lo(tt), D::add(zw[p], D::off_lo())), sw[p]);  // k = 2j
+          hi[p] = D::mul(D::sub(D::hi(tt), D::add(zw[p], D::off_hi())), sw[p]);  // k = 2j + 1
+        }
+        // MN-major swizzled tile: atom cg / 8 (64 columns), row k, 16-byte chunk (cg % 8) ^ (k % 8)
+        uint8_t* b = st + kBOff + (cg >> 3) * 8192;
+        const int k0 = 2 * j, k1 = 2 * j + 1;
+        *reinterpret_cast<uint4*>(b + k0 * 128 + (((cg & 7) ^ (k0 & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(b + k1 * 128 + (((cg & 7) ^ (k1 & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      // make the generic-proxy stores visible to the tensor core, then signal
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bready[slot]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (mbar_wait_bounded(accum, 0u, args.err, 8)) {
+      tc_fence_after();
+      pdl_wait();  // output writes follow the previous kernel
+      const int rw = 32 * warp + lane;  // row within a row tile = TMEM lane
+      for (int t = 0; t < tiles; ++t) {
+        const int m = m0 + t * kMT + rw;
+        for (int cc = 0; cc < kN; cc += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + t * kN + cc, r);
+          if (m < args.M) {
+            XT* dst = static_cast<XT*>(args.out) + (int64_t)m * args.ldo + n0 + cc;
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const int col = n0 + cc + e;
+              if (col + 1 < args.N) {
+                float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
+                if (args.bias) {
+                  v0 += load_as_f32(args.bias, col, args.bias_dtype);
+                  v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
+                }
+                dst[e] = Num<XT>::from_f(v0);
+                dst[e + 1] = Num<XT>::from_f(v1);
+              } else if (col < args.N) {
+                float v0 = round_to<XT>(__uint_as_float(r[e]));
+                if (args.bias) v0 += load_as_f32(args.bias, col, args.bias_dtype);
+                dst[e] = Num<XT>::from_f(v0);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+}  // namespace tc
+
+bool gemm_supported(const QLinearProblem& pb) {
+  if (pb.M <= 32) return false;
+  if (!(pb.x_dtype == TF_F16 || pb.x_dtype == TF_BF16) || pb.param_dtype != pb.x_dtype) return false;
+  if (pb.group_size % 64 != 0 || pb.K % 64 != 0 || pb.K == 0 || pb.K_pad % 64 != 0) return false;
+  if (pb.N % 16 != 0 || pb.ldx % 8 != 0) return false;
+  if (!aligned(pb.x, 16) || !aligned(pb.packed, 16) || !aligned(pb.scales, 16) || !aligned(pb.zeros, 16))
+    return false;
+  if (pb.M > 0x7fffffffLL || pb.N > 0x7fffffffLL) return false;
+  return true;
+}
+
 size_t gemm_workspace_bytes(int64_t, int64_t, int64_t) { return kWsHeader; }
-int gemm_launch(const QLinearProblem&, cudaStream_t) {
-  return fail(TF_ERR_UNSUPPORTED, "qlinear: tcgen05 GEMM regime not built");
+
+template <typename XT>
+static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
+  using namespace tc;
+  auto kern = gemm_int4_tc_kernel<XT>;
+  const size_t smem = (size_t)kStages * kStage + 1024 + 128;
+  static bool attr_set[64] = {false};  // per element type and device
+  const int dev = current_device() & 63;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("gemm set smem attribute");
+    attr_set[dev] = true;
+  }
+  return launch_ex("gemm_int4_tc", kern, grid, dim3(kThreads), smem, st, dim3(1, 1, 1), maps[0], maps[1], maps[2],
+                   maps[3], a);
+}
+
+int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
+  using namespace tc;
+  if (!pb.workspace || pb.workspace_bytes < kWsHeader)
+    return fail(TF_ERR_WORKSPACE, "qlinear(gemm): workspace %zu bytes < required %zu", pb.workspace_bytes,
+                (size_t)kWsHeader);
+  CUtensorMap maps[4];
+  // x [M rows, K] halves, box 64 k x 128 rows, 128-byte swizzle (K-major UMMA layout)
+  int rc = encode_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, (uint64_t)pb.K, (uint64_t)pb.M,
+                                (uint64_t)pb.ldx * 2, kKC, kMT, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // packed weights [K_pad/2 rows, N bytes], box 128 columns x 32 rows
+  rc = encode_tensor_map_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, pb.packed, (uint64_t)pb.N,
+                            (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, kN, kKC / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  const int64_t groups = pb.K_pad / pb.group_size;
+  rc = encode_tensor_map_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.scales, (uint64_t)pb.N, (uint64_t)groups,
+                            (uint64_t)pb.N * 2, kN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.zeros, (uint64_t)pb.N, (uint64_t)groups,
+                            (uint64_t)pb.N * 2, kN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  Args a{};
+  a.bias = pb.bias;
+  a.bias_dtype = pb.bias_dtype;
+  a.out = pb.out;
+  a.ldo = pb.ldo;
+  a.err = reinterpret_cast<int*>(pb.workspace);
+  a.M = (int)pb.M;
+  a.N = (int)pb.N;
+  a.n_chunks = (int)(pb.K / kKC);  // x is zero beyond K: chunks past it add nothing
+  a.group_size = pb.group_size;
+  const uint32_t ab = pb.x_dtype == TF_BF16 ? 1u : 0u;
+  // fp32 accumulator (bit 4), A/B type (bits 7-9, 10-12), A K-major (bit 15 = 0),
+  // B MN-major (bit 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28)
+  a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (1u << 16) | ((uint32_t)(kN >> 3) << 17) |
+            ((uint32_t)(kMT >> 4) << 24);
+  const dim3 grid((unsigned)cdiv(pb.N, kN), (unsigned)cdiv(pb.M, (int64_t)kMT * kMaxTiles));
+  if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16>(grid, maps, a, st);
+  return launch_gemm<__half>(grid, maps, a, st);
 }
 
 }  // namespace tf
