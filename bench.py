@@ -375,11 +375,13 @@ def run_ours(args) -> None:
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        torch.cuda.nvtx.range_push("timed_decode")  # lets a profiler select exactly the timed steps
         e0.record()
         for _ in range(args.steps):
             dec.graph.replay()
         e1.record()
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
@@ -411,6 +413,16 @@ def run_ours(args) -> None:
     peaks = _peaks()
     roof = gemv_roofline(dec, peaks["hbm_gbs"])
     roof["peak_source"] = peaks["source"]
+    # DRAM traffic: an ncu capture of one GEMV launch (read + write bytes over
+    # its algorithmic bytes, committed under profiles/), scaled to the step
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_dram_traffic.json")) as f:
+            tr = json.load(f)
+        roof["traffic"] = tr["ratio"] * roof["algorithmic_bytes_per_step"]
+        roof["traffic_unit"] = "bytes per step"
+        roof["traffic_source"] = f"ncu dram bytes / algorithmic bytes = {tr['ratio']:.4f} on {tr['case']}"
+    except (OSError, KeyError, ValueError):
+        pass
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
