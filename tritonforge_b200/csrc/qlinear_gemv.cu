@@ -55,7 +55,10 @@ constexpr int kWRows = kStageK / 2;        // packed rows per stage
 constexpr int kWBoxBytes = kWRows * kCols; // 16 KiB
 constexpr int kMaxCluster = 8;
 constexpr int kRedPitch = kCols + 4;       // floats per row of the smem reduction tiles
-constexpr int kWarps = 12;                 // consumer warps per CTA
+#ifndef TF_GEMV_WARPS
+#define TF_GEMV_WARPS 12
+#endif
+constexpr int kWarps = TF_GEMV_WARPS;      // consumer warps per CTA
 constexpr int kCW = 64;                    // columns of one warp unit
 constexpr int kSpan = kCW / 8;             // packed bytes (columns) per thread and row
 constexpr int kTiles = kCW / 16;           // 16-column MMA tiles of a unit
@@ -502,6 +505,41 @@ static void fill_ring(Plan& p) {
   p.smem = ring + 1024 + 2 * S * 8 + 64;
 }
 
+// Clusters of `ks` CTAs that can be resident at once (thread-block clusters
+// are placed within one GPC, so sizes that do not divide a GPC's SMs leave
+// SMs idle); cached per device, token-tile count and cluster size.
+template <int NT>
+static int active_clusters(int ks, size_t smem) {
+  static int cache[64][kMaxCluster + 1] = {};
+  const int dev = current_device() & 63;
+  int& c = cache[dev][ks];
+  if (c > 0) return c;
+  auto kern = gemv_int4_kernel<__nv_bfloat16, __nv_bfloat16, NT>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, (unsigned)ks, 1);
+    cfg.blockDim = dim3(32 * (kWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = (unsigned)ks;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  if (n <= 0) n = num_sms() / ks;
+  c = n;
+  return n;
+}
+
+static int active_clusters_nt(int nt, int ks, size_t smem) {
+  return nt == 1 ? active_clusters<1>(ks, smem) : (nt == 2 ? active_clusters<2>(ks, smem) : active_clusters<4>(ks, smem));
+}
+
 static Plan make_plan(int64_t M, int64_t N, int64_t K_pad) {
   Plan p{};
   p.nt = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
@@ -512,15 +550,17 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K_pad) {
   else fill_ring<4>(p);
   // Split K (a cluster of ks CTAs per column block). A CTA's time is about
   // its stage count plus a fixed ramp (pipeline fill and the reduction, worth
-  // ~4 stages), and CTAs run in waves of one per SM: pick the split with the
-  // least waves x (stages per CTA + ramp), the smallest split on ties.
-  const int64_t slots = num_sms();
+  // ~4 stages), and CTAs run in waves of as many clusters as can be resident
+  // at once: pick the split with the least waves x (stages per CTA + ramp),
+  // the smallest split on ties.
   int64_t ks = 1;
   int64_t best = -1;
   for (int64_t k = 1; k <= kMaxCluster && k <= p.n_stages; ++k) {
     const int64_t spc_k = cdiv(p.n_stages, k);
-    const int64_t ctas = p.n_cb * cdiv(p.n_stages, spc_k);
-    const int64_t cost = cdiv(ctas, slots) * (spc_k + 4);
+    const int64_t ks_eff = cdiv(p.n_stages, spc_k);
+    if (ks_eff != k) continue;  // this split is the same as a smaller one
+    const int64_t resident = (int64_t)active_clusters_nt(p.nt, (int)k, p.smem);  // clusters at once
+    const int64_t cost = cdiv(p.n_cb, resident) * (spc_k + 4);
     if (best < 0 || cost < best) {
       best = cost;
       ks = k;
