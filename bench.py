@@ -274,6 +274,8 @@ def run_reference(args) -> None:
 def _config(args) -> dict:
     tp = args.model != "0.5b"
     par = (f"tp{args.gpus}" if tp else f"replicas{args.gpus}") if args.gpus > 1 else "single"
+    if tp and args.gpus > 1:
+        par += "+fused-allreduce-rmsnorm" if args.allreduce == "fused" else "+nccl-allreduce"
     return {"workload": f"Qwen2.5-{args.model.upper()}-shaped int4 g128 greedy decode", "model": f"qwen2.5-{args.model}",
             "batch_per_gpu": args.batch, "prompt_len": args.prompt,
             "global_batch": args.batch if tp else args.batch * args.gpus, "parallelism": par,
@@ -351,7 +353,8 @@ def run_ours(args) -> None:
                                         seed=0)
         max_len = args.prompt + args.warmup + 2 * args.steps + 8
         group = dist.group.WORLD if world > 1 else None
-        dec = QwenDecoder(weights, batch=args.batch, max_len=max_len, group=group)
+        dec = QwenDecoder(weights, batch=args.batch, max_len=max_len, group=group,
+                          fused_allreduce=args.allreduce == "fused")
         dec.fill_cache(args.prompt, seed=1)
     else:
         args.want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
@@ -452,6 +455,8 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if dec.allreduce_errors():
+        raise RuntimeError(f"fused all-reduce reported device error bits {dec.allreduce_errors()}")
     dec.release()
     del dec
     if world > 1:
@@ -469,6 +474,8 @@ def main() -> None:
                     help="72b/7b: tensor parallel across the GPUs; 0.5b: transformers model, one replica per GPU")
     ap.add_argument("--batch", type=int, default=None, help="sequences (default 32 for 72b/7b, 8 for 0.5b)")
     ap.add_argument("--prompt", type=int, default=None, help="context length (default 4096 / 2048 / 128)")
+    ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
+                    help="tensor parallel: fused all-reduce + RMSNorm over peer memory, or NCCL + RMSNorm")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -181,6 +181,27 @@ int tf_decode_attention(const void* q, const void* k_cache, const void* v_cache,
 int tf_swiglu_strided(const void* gate, const void* up, void* out, int64_t M, int64_t N, int64_t ldg,
                       int64_t ldu, int64_t ldo, int dtype, void* stream);
 
+/* tf_allreduce_rmsnorm_residual: tensor-parallel all-reduce of row-parallel
+ * partial sums fused with residual-add + RMSNorm (no reference counterpart:
+ * the reference is single-GPU; it replaces an all-reduce followed by
+ * rmsnorm_residual, reference integration/qwen.py:145-150 / kernels
+ * rmsnorm_residual.py:141-151).
+ *   peer_buffers[r]      device address of rank r's symmetric buffer (device array)
+ *   peer_signal_pads[r]  device address of rank r's signal pad of u32 slots (device array)
+ *   offset_bytes         this call's partial tile [M, N] inside every buffer
+ *   pad_slot             first signal-pad slot used (pad_slot .. pad_slot + world - 1)
+ *   counters             this rank's device u32[2], zeroed once before the first call
+ * Computes o = round(sum_r partial_r) (fp32 sum in rank order, identical on
+ * every rank), summed = round(o + residual), normed = round(round(summed *
+ * rstd) * weight). Waits for the peers' signals at most 1 s; on expiry sets
+ * bit 16 of *error_word and still returns TF_OK (read the word to check).
+ * N % 8 == 0, N <= 16384. */
+int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const uint64_t* peer_signal_pads,
+                                  int64_t offset_bytes, int32_t pad_slot, int32_t rank, int32_t world,
+                                  uint32_t* counters, const void* residual, const void* weight, int w_dtype,
+                                  void* normed, void* summed, int64_t M, int64_t N, float eps, int dtype,
+                                  int* error_word, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

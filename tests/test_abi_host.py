@@ -146,3 +146,14 @@ def test_no_cpu_fallback():
         kernels.swiglu(torch.randn(4, 8, dtype=torch.float16), torch.randn(4, 8, dtype=torch.float16))
     with pytest.raises(RuntimeError, match="CUDA"):
         quant.quantize_int4_group(torch.randn(4, 128), 128)
+
+
+def test_allreduce_rmsnorm_validates_without_a_gpu():
+    lib = _lib.load()
+    # null pointers / rank outside the group are rejected before anything is launched
+    assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 0, 2, None, None, None, _lib.BF16, None, None, 4,
+                                             8192, 1e-6, _lib.BF16, None, None) == _lib.ERR_BAD_ARG
+    assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 3, 2, None, None, None, _lib.BF16, None, None, 4,
+                                             8192, 1e-6, _lib.BF16, None, None) == _lib.ERR_BAD_SHAPE
+    assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 0, 2, None, None, None, _lib.BF16, None, None, 0,
+                                             8192, 1e-6, _lib.BF16, None, None) == _lib.OK

@@ -78,15 +78,17 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_nccl_matches_tp1():
+@pytest.mark.parametrize("fused", ["1", "0"])
+def test_tp_nccl_matches_tp1(fused):
     n = 2 if torch.cuda.device_count() < 4 else 4
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(root, "tests", "tp_check.py")]
-    env = dict(os.environ, TP_CHECK_MODEL="72b" if n == 4 else "7b", TP_CHECK_LAYERS="1")
+    env = dict(os.environ, TP_CHECK_MODEL="72b" if n == 4 else "7b", TP_CHECK_LAYERS="1", TP_CHECK_FUSED=fused,
+               NCCL_NVLS_ENABLE="0")
     p = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
     lines = [l for l in p.stdout.splitlines() if l.startswith("TP_CHECK ")]
     assert p.returncode == 0 and lines, p.stdout[-3000:] + p.stderr[-3000:]
     rep = json.loads(lines[-1][len("TP_CHECK "):])
-    assert rep["ok"] and rep["ranks_identical"], rep
+    assert rep["ok"] and rep["ranks_identical"] and rep["fused_allreduce"] == (fused == "1"), rep

@@ -101,7 +101,8 @@ def _nccl_main() -> int:
     full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=3, layers=layers)
     ref = QwenDecoder(full, B, T)
     ref.fill_cache(40, seed=5)  # same seed on every rank -> same cache everywhere
-    dec = QwenDecoder(full.shard(world, rank), B, T, group=dist.group.WORLD)
+    fused = os.environ.get("TP_CHECK_FUSED", "1") == "1"  # fused all-reduce + RMSNorm, or NCCL
+    dec = QwenDecoder(full.shard(world, rank), B, T, group=dist.group.WORLD, fused_allreduce=fused)
     copy_cache(ref, dec, world, rank)
     report = {"rank": rank, "ok": True, "steps": []}
     dec.capture()
@@ -125,6 +126,9 @@ def _nccl_main() -> int:
         same_all &= all(torch.equal(gathered[0], g) for g in gathered)
         dec.tokens.copy_(ref.tokens)  # keep the two decodes on the same tokens
     report["ranks_identical"] = same_all
+    report["fused_allreduce"] = dec.fused_allreduce
+    report["allreduce_errors"] = dec.allreduce_errors()
+    report["ok"] &= report["allreduce_errors"] == 0
     report["ok"] &= report["ranks_identical"]
     torch.cuda.synchronize()
     dec.release()

@@ -240,7 +240,8 @@ class QwenDecoder:
     `group` is a torch.distributed process group, or any object with an
     `all_reduce(tensor)` method that sums in place across the ranks."""
 
-    def __init__(self, model_or_weights, batch: int, max_len: int, group=None, vocab_parallel: bool | None = None):
+    def __init__(self, model_or_weights, batch: int, max_len: int, group=None, vocab_parallel: bool | None = None,
+                 fused_allreduce: bool | None = None):
         w = model_or_weights if isinstance(model_or_weights, QwenWeights) else QwenWeights.from_hf(model_or_weights)
         self.w = w
         self.model = w.model
@@ -254,6 +255,9 @@ class QwenDecoder:
 
             self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         self.vocab_parallel = (self.world > 1) if vocab_parallel is None else (vocab_parallel and self.world > 1)
+        # Fused all-reduce + residual + RMSNorm over peer memory (tf_allreduce_rmsnorm_residual)
+        # in place of an NCCL all-reduce followed by rmsnorm_residual.
+        self.fused_allreduce = (self.world > 1) if fused_allreduce is None else (fused_allreduce and self.world > 1)
         self.B, self.T = batch, max_len
         self.H, self.I = w.hidden, w.inter
         self.Hq, self.Hkv, self.D = w.q_heads, w.kv_heads, w.head_dim
@@ -291,6 +295,8 @@ class QwenDecoder:
             "mlp": torch.empty(B, self.H, dtype=dt, device=dev),
             "logits": torch.empty(B, self.lm_head.shape[0], dtype=dt, device=dev),
         }
+        if self.fused_allreduce:
+            self._setup_symmetric(B)
         if self.vocab_parallel:
             self.buf["best"] = torch.empty(B, 2, dtype=torch.float32, device=dev)     # (logit, token id)
             self.buf["all_best"] = torch.empty(self.world, B, 2, dtype=torch.float32, device=dev)
@@ -298,6 +304,49 @@ class QwenDecoder:
         self.graph: torch.cuda.CUDAGraph | None = None
         self._lib = _lib.load()
         self._dt = _lib.dtype_code(dt)
+
+    # ---------------------------------------------------- fused all-reduce
+    PAD_SLOT = 64  # first signal-pad slot this decoder uses
+
+    def _setup_symmetric(self, B: int) -> None:
+        """Symmetric buffer holding the o_proj and down_proj partial tiles
+        (they alternate, which makes buffer reuse safe without a second
+        barrier), peer pointers and signal pads (torch symmetric memory)."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        n = B * self.H
+        gname = self.group.group_name
+        if hasattr(symm, "is_symm_mem_enabled_for_group") and not symm.is_symm_mem_enabled_for_group(gname):
+            symm.enable_symm_mem_for_group(gname)
+        sbuf = symm.empty(2 * n, dtype=self.dtype, device=self.dev)
+        hdl = symm.rendezvous(sbuf, self.group)
+        if hdl.signal_pad_size < 4 * (self.PAD_SLOT + self.world):
+            raise RuntimeError("symmetric-memory signal pad too small")
+        hdl.get_signal_pad(hdl.rank, (self.PAD_SLOT + self.world,), torch.int32)[self.PAD_SLOT:].zero_()
+        self._symm = (sbuf, hdl)
+        self.buf["o"] = sbuf[:n].view(B, self.H)
+        self.buf["mlp"] = sbuf[n:].view(B, self.H)
+        esz = sbuf.element_size()
+        base = int(hdl.offset)  # this tensor's offset inside every rank's buffer
+        self._ar_off = {"o": base, "mlp": base + n * esz}
+        self._ar_ctr = torch.zeros(2, dtype=torch.int32, device=self.dev)
+        self._ar_err = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+
+    def _ar_norm(self, which: str, res: torch.Tensor, weight: torch.Tensor, normed: torch.Tensor,
+                 summed: torch.Tensor) -> None:
+        _, hdl = self._symm
+        _lib.check(self._lib.tf_allreduce_rmsnorm_residual(
+            hdl.buffer_ptrs_dev, hdl.signal_pad_ptrs_dev, self._ar_off[which], self.PAD_SLOT, self.rank, self.world,
+            self._ar_ctr.data_ptr(), res.data_ptr(), weight.data_ptr(), _lib.dtype_code(weight.dtype),
+            normed.data_ptr(), summed.data_ptr(), self.B, self.H, self.eps, self._dt, self._ar_err.data_ptr(),
+            _lib.stream_ptr(self.dev)), "allreduce_rmsnorm_residual")
+
+    def allreduce_errors(self) -> int:
+        """Device error bits of the fused all-reduce (16: a peer's signal did not arrive within 1 s)."""
+        return int(self._ar_err.item()) if self.fused_allreduce else 0
 
     # ------------------------------------------------------------------ step
     def _lin(self, x: torch.Tensor, ql: QuantLinear, out: torch.Tensor) -> torch.Tensor:
@@ -328,7 +377,10 @@ class QwenDecoder:
                 kernels.rmsnorm(b["x"], L["in_norm"], self.eps, out=b["normed"])
                 res.copy_(b["x"])
             else:
-                kernels.rmsnorm_residual(b["mlp"], res, L["in_norm"], self.eps, out=(b["normed"], res_next))
+                if self.fused_allreduce:
+                    self._ar_norm("mlp", res, L["in_norm"], b["normed"], res_next)
+                else:
+                    kernels.rmsnorm_residual(b["mlp"], res, L["in_norm"], self.eps, out=(b["normed"], res_next))
                 res, res_next = res_next, res
             self._lin(b["normed"], L["qkv"], b["qkv"])
             _lib.check(lib.tf_rope_kv_append(
@@ -340,8 +392,11 @@ class QwenDecoder:
                 b["attn"].data_ptr(), lenp, self.B, self.Hq, self.Hkv, self.D, self.T, self.scale,
                 self._dt, st), "decode_attention")
             self._lin(b["attn"], L["o"], b["o"])
-            self._all_reduce(b["o"])
-            kernels.rmsnorm_residual(b["o"], res, L["post_norm"], self.eps, out=(b["normed"], res_next))
+            if self.fused_allreduce:
+                self._ar_norm("o", res, L["post_norm"], b["normed"], res_next)
+            else:
+                self._all_reduce(b["o"])
+                kernels.rmsnorm_residual(b["o"], res, L["post_norm"], self.eps, out=(b["normed"], res_next))
             res, res_next = res_next, res
             self._lin(b["normed"], L["gu"], b["gu"])
             gu = b["gu"]
@@ -349,8 +404,12 @@ class QwenDecoder:
                 gu.data_ptr(), gu.data_ptr() + self.I * gu.element_size(), b["act"].data_ptr(), self.B, self.I,
                 gu.stride(0), gu.stride(0), b["act"].stride(0), self._dt, st), "swiglu")
             self._lin(b["act"], L["down"], b["mlp"])
-            self._all_reduce(b["mlp"])
-        kernels.rmsnorm_residual(b["mlp"], res, self.final_norm, self.eps, out=(b["normed"], res_next))
+            if not self.fused_allreduce:
+                self._all_reduce(b["mlp"])
+        if self.fused_allreduce:
+            self._ar_norm("mlp", res, self.final_norm, b["normed"], res_next)
+        else:
+            kernels.rmsnorm_residual(b["mlp"], res, self.final_norm, self.eps, out=(b["normed"], res_next))
         torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
         if self.vocab_parallel:
             self._vocab_parallel_argmax()
@@ -397,8 +456,12 @@ class QwenDecoder:
         self.graph = g
 
     def release(self) -> None:
-        """Drop the captured graph (before destroying a process group it uses)."""
+        """Drop the captured graph (before destroying a process group it uses)
+        and the symmetric buffer."""
         self.graph = None
+        if getattr(self, "_symm", None) is not None:
+            torch.cuda.synchronize(self.dev)
+            self._symm = None
 
     def replay(self) -> torch.Tensor:
         if self.graph is None:
