@@ -21,7 +21,7 @@ from tritonforge_b200.decode import QwenDecoder, QwenWeights
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name,tp,layers", [("7b", 2, 2), ("72b", 4, 1), ("72b", 2, 1)])
+@pytest.mark.parametrize("name,tp,layers", [("7b", 2, 2), ("72b", 4, 1), ("72b", 2, 1), ("72b", 8, 1)])
 def test_tp_threads_match_tp1(name, tp, layers):
     dev = torch.device("cuda", 0)
     B, T, steps = 3, 64, 3

@@ -21,12 +21,16 @@
 // which each peer does only after finishing its reads of that tile.
 // The call count lives in device memory (advanced by the last CTA of each
 // call) so the kernel can be replayed from a CUDA graph.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tf {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 
 template <typename T>
 struct V8 {
@@ -66,19 +70,25 @@ struct ArArgs {
   float eps;
 };
 
+// One cluster of `gridDim.y` CTAs per row: CTA c reduces and normalises
+// columns [c * 8 * VPT * kThreads, ...) of the row, the row's sum of squares is
+// combined through distributed shared memory in CTA-rank order.
 template <typename T, typename TW, int VPT>
 __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, const T* __restrict__ residual,
                                                               const TW* __restrict__ weight, T* __restrict__ normed,
                                                               T* __restrict__ summed) {
   __shared__ float red[32];
+  __shared__ float part_ss;
   __shared__ uint32_t target_s;
   __shared__ int ok_s;
   pdl_trigger();
   pdl_wait();  // this rank's partial (the previous kernel's output) is complete
   const int64_t row = blockIdx.x;
+  const int cta_cols = 8 * VPT * kThreads;
+  const int c0 = blockIdx.y * cta_cols;  // first column of this CTA
   if (threadIdx.x == 0) {
     const uint32_t target = *reinterpret_cast<volatile uint32_t*>(a.counters) + 1u;
-    if (blockIdx.x == 0) {
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
       __threadfence_system();  // the partial is visible to peers before the signal
       for (int p = 0; p < a.world; ++p)
         red_release_sys_add(reinterpret_cast<uint32_t*>(a.pads[p]) + a.pad_slot + a.rank, 1u);
@@ -99,24 +109,30 @@ __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, co
     ok_s = ok;
   }
   __syncthreads();
-  const int nvec = a.n >> 3;
-  if (ok_s) {
-    V8<T> s[VPT];
-    float ss = 0.f;
+  const int ok = ok_s;
+  V8<T> s[VPT];
+  float ss = 0.f;
+  if (ok) {
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
-      const int vi = threadIdx.x + v * kThreads;
-      if (vi < nvec) {
+      const int col = c0 + 8 * (threadIdx.x + v * kThreads);
+      if (col < a.n) {
+        // issue the loads of up to 8 peers before using any (NVLink latency)
+        const int64_t off = a.offset + (row * a.n + col) * (int64_t)sizeof(T);
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const int64_t off = a.offset + (row * a.n + (int64_t)vi * 8) * (int64_t)sizeof(T);
-        for (int p = 0; p < a.world; ++p) {
-          V8<T> part;
-          part.raw = ld_peer(reinterpret_cast<const uint8_t*>(a.bufs[p]) + off);
+        for (int p0 = 0; p0 < a.world; p0 += 8) {
+          V8<T> part[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += part.get(e);
+          for (int p = 0; p < 8; ++p)
+            if (p0 + p < a.world) part[p].raw = ld_peer(reinterpret_cast<const uint8_t*>(a.bufs[p0 + p]) + off);
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            if (p0 + p < a.world)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[e] += part[p].get(e);  // rank order
         }
         V8<T> r;
-        r.raw = *reinterpret_cast<const uint4*>(residual + row * a.n + (int64_t)vi * 8);
+        r.raw = *reinterpret_cast<const uint4*>(residual + row * a.n + col);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float o = round_to<T>(acc[e]);
@@ -124,36 +140,50 @@ __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, co
           const float f = s[v].get(e);
           ss = fmaf(f, f, ss);
         }
-        *reinterpret_cast<uint4*>(summed + row * a.n + (int64_t)vi * 8) = s[v].raw;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    float tot = lane < kThreads / 32 ? red[lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    const float rstd = 1.0f / sqrtf(tot / (float)a.n + a.eps);
-#pragma unroll
-    for (int v = 0; v < VPT; ++v) {
-      const int vi = threadIdx.x + v * kThreads;
-      if (vi < nvec) {
-        V8<T> out;
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          out.set(e, round_to<T>(s[v].get(e) * rstd) * Num<TW>::to_f(weight[(int64_t)vi * 8 + e]));
-        *reinterpret_cast<uint4*>(normed + row * a.n + (int64_t)vi * 8) = out.raw;
+        *reinterpret_cast<uint4*>(summed + row * a.n + col) = s[v].raw;
       }
     }
   }
-  // the last CTA of the call advances the call count
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+    part_ss = t;
+  }
+  const bool clustered = gridDim.y > 1;  // a single CTA per row needs no cluster
+  cg::cluster_group cluster = cg::this_cluster();
+  if (clustered) cluster.sync();
+  else __syncthreads();
+  if (ok) {
+    float tot = 0.f;
+    if (clustered) {
+      for (int c = 0; c < (int)gridDim.y; ++c) tot += *cluster.map_shared_rank(&part_ss, c);
+    } else {
+      tot = part_ss;
+    }
+    const float rstd = 1.0f / sqrtf(tot / (float)a.n + a.eps);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int col = c0 + 8 * (threadIdx.x + v * kThreads);
+      if (col < a.n) {
+        V8<T> out;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          out.set(e, round_to<T>(s[v].get(e) * rstd) * Num<TW>::to_f(weight[col + e]));
+        *reinterpret_cast<uint4*>(normed + row * a.n + col) = out.raw;
+      }
+    }
+  }
+  if (clustered) cluster.sync();  // peers may still read this CTA's partial sum of squares
+  // the last CTA of the call advances the call count
   if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t done = atomicAdd(a.counters + 1, 1u);
-    if (done == gridDim.x - 1) {
+    if (done == gridDim.x * gridDim.y - 1) {
       a.counters[1] = 0u;
       a.counters[0] = target_s;
       __threadfence();
@@ -164,22 +194,19 @@ __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, co
 template <typename T, typename TW>
 int launch_ar(const ArArgs& a, const void* residual, const void* weight, void* normed, void* summed, int64_t m,
               cudaStream_t st) {
-  const int nvec = a.n / 8;
   const T* r = static_cast<const T*>(residual);
   const TW* w = static_cast<const TW*>(weight);
   T* no = static_cast<T*>(normed);
   T* su = static_cast<T*>(summed);
-  if (nvec <= kThreads)
-    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 1>, dim3((unsigned)m), dim3(kThreads), 0, st,
-                     dim3(1, 1, 1), a, r, w, no, su);
-  if (nvec <= 2 * kThreads)
-    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 2>, dim3((unsigned)m), dim3(kThreads), 0, st,
-                     dim3(1, 1, 1), a, r, w, no, su);
-  if (nvec <= 4 * kThreads)
-    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 4>, dim3((unsigned)m), dim3(kThreads), 0, st,
-                     dim3(1, 1, 1), a, r, w, no, su);
-  return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 8>, dim3((unsigned)m), dim3(kThreads), 0, st,
-                   dim3(1, 1, 1), a, r, w, no, su);
+  // a cluster of up to 8 CTAs per row, each 128 threads x 8 columns x VPT
+  if (a.n <= 8 * 8 * kThreads) {
+    const unsigned c = (unsigned)cdiv(a.n, 8 * kThreads);
+    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 1>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
+                     dim3(1, c, 1), a, r, w, no, su);
+  }
+  const unsigned c = (unsigned)cdiv(a.n, 2 * 8 * kThreads);
+  return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 2>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
+                   dim3(1, c, 1), a, r, w, no, su);
 }
 
 }  // namespace
@@ -196,7 +223,7 @@ extern "C" int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const
   if (M == 0 || N == 0) return TF_OK;
   if (!peer_buffers || !peer_signal_pads || !counters || !residual || !weight || !normed || !summed || !error_word)
     return fail(TF_ERR_BAD_ARG, "allreduce_rmsnorm: null pointer");
-  if (N % 8 != 0 || N > 8 * 8 * 256) return fail(TF_ERR_UNSUPPORTED, "allreduce_rmsnorm: N=%lld", (long long)N);
+  if (N % 8 != 0 || N > 2 * 8 * 8 * 128) return fail(TF_ERR_UNSUPPORTED, "allreduce_rmsnorm: N=%lld", (long long)N);
   if (offset_bytes % 16 || !aligned(residual, 16) || !aligned(normed, 16) || !aligned(summed, 16))
     return fail(TF_ERR_UNALIGNED, "allreduce_rmsnorm: 16-byte alignment required");
   if (M > 0x7fffffffLL) return fail(TF_ERR_BAD_SHAPE, "allreduce_rmsnorm: too many rows");
