@@ -295,11 +295,14 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
     launches = []
     for L in dec.layers:
         launches += [(b["normed"], L["qkv"], b["qkv"]), (b["attn"], L["o"], b["o"]),
-                     (b["normed"], L["gu"], b["gu"]), (b["act"], L["down"], b["mlp"])]
+                     (b["normed"], L["gu"], b["act"]), (b["act"], L["down"], b["mlp"])]
 
     def run():
         for x, ql, out in launches:
-            kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
+            if ql is not None and out is b["act"]:
+                dec._gate_up(x, ql, out)  # fused gate|up + SwiGLU (the step's own launch)
+            else:
+                kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
 
     s = torch.cuda.Stream(dec.dev)
     with torch.cuda.stream(s):
@@ -323,7 +326,7 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
     for x, ql, out in launches:
         m, k = x.shape
         kp, n = ql.packed.shape[0] * 2, ql.packed.shape[1]
-        alg += m * k * 2 + kp * n // 2 + 2 * (kp // ql.group_size) * n * 2 + m * n * 2
+        alg += m * k * 2 + kp * n // 2 + 2 * (kp // ql.group_size) * n * 2 + out.numel() * out.element_size()
         if ql.bias is not None:
             alg += n * 2
     achieved = alg / (total_us * 1e-6) / 1e9

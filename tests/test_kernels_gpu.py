@@ -262,3 +262,52 @@ def test_gemm_regime(m, n, k, dtype):
     assert_rms_close(out[rows.cuda()], ref, dtype, f"gemm {m}x{n}x{k}")
     again = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemm"})
     assert torch.equal(out, again), "deterministic"
+
+
+# ---- fused gate|up + SwiGLU (decode regime) --------------------------------
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,i,k", [(1, 4864, 896), (8, 4864, 896), (3, 896, 4864), (16, 18944, 3584),
+                                   (32, 7424, 8192), (5, 1024, 29568)])
+def test_qlinear_swiglu(m, i, k, dtype):
+    from tritonforge_b200.tp import interleave_gate_up
+
+    g = torch.Generator().manual_seed(m + i)
+    x = torch.randn(m, k, generator=g).to(dtype).cuda()
+    wg = (torch.randn(i, k, generator=g) * 0.02).cuda()
+    wu = (torch.randn(i, k, generator=g) * 0.02).cuda()
+    pg, sg, zg, _ = quant.quantize_int4_group(wg, GROUP, dtype)
+    pu, su, zu, _ = quant.quantize_int4_group(wu, GROUP, dtype)
+    packed = interleave_gate_up(pg, pu).contiguous()
+    scales = interleave_gate_up(sg, su).contiguous()
+    zeros = interleave_gate_up(zg, zu).contiguous()
+    out = torch.full((m, i), float("nan"), dtype=dtype, device="cuda")
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    rc = _lib.load().tf_qlinear_swiglu(x.data_ptr(), x.stride(0), _lib.dtype_code(dtype), packed.data_ptr(),
+                                       scales.data_ptr(), zeros.data_ptr(), _lib.dtype_code(dtype), out.data_ptr(),
+                                       out.stride(0), m, 2 * i, k, packed.shape[0] * 2, GROUP, ws.data_ptr(),
+                                       ws.numel(), _lib.stream_ptr(x.device))
+    _lib.check(rc, "qlinear_swiglu")
+    gate = oracle_linear(x, pg, sg, zg, None)  # the separate projections, rounded to the dtype
+    up = oracle_linear(x, pu, su, zu, None)
+    ref = oops.swiglu(gate, up, NP_DT[dtype])
+    got = f32(out).astype(np.float64)
+    assert np.isfinite(got).all()
+    # The kernel rounds gate and up exactly where the oracle does, but its fp32
+    # accumulation order differs, so a projection may land one ulp away; the
+    # product then moves by that ulp times the other factor. Allowed per
+    # element: the contract's tolerance, or that one-ulp propagation plus one
+    # ulp of the output.
+    g64, u64, r64 = gate.astype(np.float64), up.astype(np.float64), ref.astype(np.float64)
+    mant = 11 if dtype == torch.float16 else 8
+
+    def ulp(v):
+        return np.ldexp(1.0, np.frexp(np.abs(v) + 1e-30)[1] - mant)
+
+    sig = 1.0 / (1.0 + np.exp(-g64))
+    dsilu = sig * (1.0 + g64 * (1.0 - sig))
+    bound = np.abs(dsilu * u64) * ulp(g64) + np.abs(g64 * sig) * ulp(u64) + ulp(r64)
+    err = np.abs(got - r64)
+    tol = (1e-2 if dtype == torch.float16 else 2e-2) * oops.rms(ref)
+    bad = (err > tol) & (err > bound)
+    assert not bad.any(), f"qlinear_swiglu {m}x{i}x{k}: {int(bad.sum())} outputs beyond tolerance, max {err.max():.4g}"
+    assert err.mean() <= 0.1 * tol, f"qlinear_swiglu {m}x{i}x{k}: mean error {err.mean():.4g}"

@@ -54,6 +54,8 @@ SIGNATURES = {
                                  _vp]),
     "tf_decode_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _f32, _i32, _vp]),
     "tf_swiglu_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "tf_qlinear_swiglu": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
+                                 _vp, _sz, _vp]),
     "tf_allreduce_rmsnorm_residual": (_i32, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp,
                                              _i64, _i64, _f32, _i32, _vp, _vp]),
 }

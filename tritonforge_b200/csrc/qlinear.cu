@@ -89,3 +89,22 @@ extern "C" int tf_workspace_error(const void* workspace, int* error_out, void* s
   if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("workspace_error sync");
   return *error_out ? TF_ERR_TIMEOUT : TF_OK;
 }
+
+extern "C" int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
+                                 const void* zeros, int param_dtype, void* out, int64_t ldo, int64_t M, int64_t N,
+                                 int64_t K, int64_t K_pad, int32_t group_size, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,     x_dtype, packed, scales, zeros, param_dtype, nullptr, 0, out, ldo,
+                    M,    N,       K,       K_pad,  group_size, workspace, workspace_bytes};
+  // validate as the projection [M, N]; the output is [M, N/2] (ldo >= N/2)
+  pb.ldo = ldo >= N ? ldo : N;
+  int rc = validate(pb);
+  if (rc != TF_OK) return rc;
+  if (ldo < N / 2) return fail(TF_ERR_BAD_SHAPE, "qlinear_swiglu: ldo %lld < N/2", (long long)ldo);
+  if (M == 0 || N == 0) return TF_OK;
+  pb.ldo = ldo;
+  if (N % 128 != 0) return fail(TF_ERR_BAD_SHAPE, "qlinear_swiglu: N=%lld not a multiple of 128", (long long)N);
+  if (!gemv_supported(pb)) return fail(TF_ERR_UNSUPPORTED, "qlinear_swiglu: needs the decode regime (M <= 32)");
+  return gemv_launch(pb, static_cast<cudaStream_t>(stream), true);
+}

@@ -29,7 +29,9 @@ struct QLinearProblem {
 
 bool gemv_supported(const QLinearProblem& pb);
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
-int gemv_launch(const QLinearProblem& pb, cudaStream_t st);
+// swiglu: the N columns are [gate 64 | up 64] per 128-column block and the
+// kernel stores round(silu(g) * u) [M, N/2] instead of the projections
+int gemv_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = false);
 
 bool gemm_supported(const QLinearProblem& pb);
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);

@@ -90,6 +90,7 @@ struct Args {
   int bias_dtype;
   int S;                // ring depth
   uint32_t tx_bytes;    // bytes the four copies of a stage deliver
+  int swiglu;           // columns are [gate 64 | up 64] per CTA: store round(silu(g) * u), 64 wide
 };
 
 // Nibble -> (offset + code) halves, exact dequantisation and the MMA.
@@ -188,6 +189,29 @@ __device__ __forceinline__ void finalize4(const Args& a, int m, int col, float4 
     float t = round_to<XT>(r[j]);
     if (a.bias) t += load_as_f32(a.bias, col + j, a.bias_dtype);
     o[j] = Num<XT>::from_f(t);
+  }
+  XT* dst = static_cast<XT*>(a.out) + (int64_t)m * a.ldo + col;
+  if (aligned(dst, 8)) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = o[j];
+  }
+}
+
+// act[m, col..col+3] = round(silu(round(g)) * round(u)) for 4 consecutive
+// intermediate columns: the gate and up projections rounded to the activation
+// type as separate linears would be (reference.py:33-35, no bias), then the
+// SwiGLU oracle's fp32 math with one rounding (reference.py:53-57)
+template <typename XT>
+__device__ __forceinline__ void finalize_swiglu4(const Args& a, int m, int col, float4 g, float4 u) {
+  const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+  __align__(8) XT o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float gr = round_to<XT>(gv[j]), ur = round_to<XT>(uv[j]);
+    const float sig = 1.0f / (1.0f + expf(-gr));
+    o[j] = Num<XT>::from_f((gr * sig) * ur);
   }
   XT* dst = static_cast<XT*>(a.out) + (int64_t)m * a.ldo + col;
   if (aligned(dst, 8)) {
@@ -451,10 +475,19 @@ __global__ void __launch_bounds__(32 * (kWarps + 1), 1)
       for (int w = 0; w < kWarps; ++w)
         if (w % kUnits % (kCols / kCW) == half)
           add4(v, reinterpret_cast<const float4*>(red + ((size_t)w * kMPad + m) * kRedPitch)[c4]);
-      if (args.ksplit == 1) {
+      if (args.ksplit == 1 && !args.swiglu) {
         if (4 * c4 < valid_cols) finalize4<XT>(args, m, n0 + 4 * c4, v);
       } else {
         reinterpret_cast<float4*>(cta + (size_t)m * kRedPitch)[c4] = v;
+      }
+    }
+    if (args.ksplit == 1 && args.swiglu) {
+      named_barrier(1, kConsumers);
+      constexpr int kHalf4 = kCols / 8;  // float4s of the gate half
+      for (int idx = tid; idx < rows * kHalf4; idx += kConsumers) {
+        const int m = idx / kHalf4, c4 = idx % kHalf4;
+        const float4* row = reinterpret_cast<const float4*>(cta + (size_t)m * kRedPitch);
+        finalize_swiglu4<XT>(args, m, blockIdx.x * (kCols / 2) + 4 * c4, row[c4], row[c4 + kHalf4]);
       }
     }
   }
@@ -463,7 +496,24 @@ __global__ void __launch_bounds__(32 * (kWarps + 1), 1)
   // split-K across the cluster: rank r finalises columns [32r/ks, 32(r+1)/ks) (in float4s)
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
-  if (warp < kWarps) {
+  if (warp < kWarps && args.swiglu) {
+    // rank r finalises gate float4s [16r/ks, 16(r+1)/ks) with their up float4s
+    constexpr int kHalf4 = kCols / 8;
+    const int ks = args.ksplit;
+    const int r = (int)cluster.block_rank();
+    const int c_lo = kHalf4 * r / ks, c_hi = kHalf4 * (r + 1) / ks;
+    const int width = c_hi - c_lo;
+    for (int idx = tid; idx < rows * width; idx += kConsumers) {
+      const int m = idx / width, c4 = c_lo + idx % width;
+      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < ks; ++j) {
+        const float4* peer = reinterpret_cast<const float4*>(cluster.map_shared_rank(cta, j) + (size_t)m * kRedPitch);
+        add4(gs, peer[c4]);
+        add4(us, peer[c4 + kHalf4]);
+      }
+      finalize_swiglu4<XT>(args, m, blockIdx.x * (kCols / 2) + 4 * c4, gs, us);
+    }
+  } else if (warp < kWarps) {
     const int ks = args.ksplit;
     const int r = (int)cluster.block_rank();
     const int c_lo = (kCols / 4) * r / ks, c_hi = (kCols / 4) * (r + 1) / ks;
@@ -612,7 +662,7 @@ static int launch_nt(const gemv::Plan& p, const CUtensorMap* maps, const gemv::A
   }
 }
 
-int gemv_launch(const QLinearProblem& pb, cudaStream_t st) {
+int gemv_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu) {
   gemv::Plan p = gemv::make_plan(pb.M, pb.N, pb.K_pad);
   if (!pb.workspace || pb.workspace_bytes < kWsHeader)
     return fail(TF_ERR_WORKSPACE, "qlinear(gemv): workspace %zu bytes < required %zu", pb.workspace_bytes,
@@ -655,6 +705,7 @@ int gemv_launch(const QLinearProblem& pb, cudaStream_t st) {
   a.rows_per_group = pb.group_size / 128;
   a.S = p.S;
   a.tx_bytes = (uint32_t)(gemv::kWBoxBytes + 4 * 8 * p.nt * 128 + 2 * (2 * gemv::kCols * 2));
+  a.swiglu = swiglu ? 1 : 0;
   const bool xh = pb.x_dtype == TF_F16, ph = pb.param_dtype == TF_F16;
   if (xh && ph) return launch_nt<__half, __half>(p, maps, a, st);
   if (!xh && !ph) return launch_nt<__nv_bfloat16, __nv_bfloat16>(p, maps, a, st);

@@ -12,16 +12,19 @@ docs/FINAL_REPORT.md:93-99). Per layer:
     decode_attention(q, cache, len=pos+1)      -> attn
     quantized_linear(attn, o)                  -> o
     rmsnorm_residual(o, residual)              -> normed, residual
-    quantized_linear(normed, [gate|up])        -> gu                    (one GEMV)
-    swiglu(gu[:, :I], gu[:, I:])               -> act
+    qlinear_swiglu(normed, [gate|up])          -> act = silu(gate) * up (one GEMV, fused epilogue)
     quantized_linear(act, down)                -> mlp_out
 
 then rmsnorm_residual(mlp_out, residual, final_norm), the tied fp16 lm_head
 (cuBLAS) and argmax. The math of each step is the reference patched model's
 (reference src/tritonforge/integration/qwen.py:101-152): the end-of-layer
 `residual + hidden` of the reference is the `summed` output of the next
-rmsnorm_residual (same rounding). q|k|v and gate|up are the reference's
-separate QuantLinear tensors concatenated along N, which changes no value.
+rmsnorm_residual (same rounding). q|k|v are the reference's separate
+QuantLinear tensors concatenated along N and gate|up interleaved per 64
+columns, which changes no value: the fused gate|up kernel rounds each
+projection to the model dtype before the SwiGLU, as the reference's separate
+launches do. With a tensor-parallel group the o_proj / down_proj all-reduce is
+fused with the following rmsnorm_residual (tf_allreduce_rmsnorm_residual).
 
 The prompt is prefilled through the patched transformers model itself and its
 KV cache copied into the static cache.
@@ -93,11 +96,25 @@ def _cat_quant(lins: list[QuantLinear]) -> QuantLinear:
                        bias, lins[0].group_size)
 
 
+def _interleave_quant(gate: QuantLinear, up: QuantLinear) -> QuantLinear:
+    """gate and up (no bias) as one QuantLinear whose columns are interleaved
+    per 64: [gate 0:64 | up 0:64 | gate 64:128 | ...] (tf_qlinear_swiglu layout)."""
+    from .tp import interleave_gate_up
+
+    if gate.bias is not None or up.bias is not None:
+        raise ValueError("gate/up projections with a bias are not supported")
+    return QuantLinear(interleave_gate_up(gate.packed, up.packed).contiguous(),
+                       interleave_gate_up(gate.scales, up.scales).contiguous(),
+                       interleave_gate_up(gate.zeros, up.zeros).contiguous(),
+                       gate.in_features, 2 * gate.out_features, None, gate.group_size)
+
+
 @dataclasses.dataclass
 class QwenWeights:
-    """Everything one rank needs to decode: per-layer int4 projections (with
-    q|k|v and gate|up concatenated along N), norms, embedding, lm_head and
-    rotary tables, with this rank's head / intermediate counts."""
+    """Everything one rank needs to decode: per-layer int4 projections (q|k|v
+    concatenated along N; gate and up interleaved per 64 columns, see
+    `_interleave_quant`), norms, embedding, lm_head and rotary tables, with
+    this rank's head / intermediate counts."""
 
     layers: list
     embed: torch.Tensor
@@ -136,7 +153,7 @@ class QwenWeights:
                 "post_norm": layer.post_attention_layernorm.weight.detach(),
                 "qkv": _cat_quant([a.q_proj, a.k_proj, a.v_proj]),
                 "o": a.o_proj,
-                "gu": _cat_quant([m.gate_proj, m.up_proj]),
+                "gu": _interleave_quant(m.gate_proj, m.up_proj),
                 "down": m.down_proj,
             })
         return cls(layers, inner.embed_tokens.weight.detach(), model.lm_head.weight.detach(),
@@ -209,7 +226,7 @@ class QwenWeights:
                 "in_norm": L["in_norm"], "post_norm": L["post_norm"],
                 "qkv": cols(L["qkv"], [(q0, q1), (nq + k0, nq + k1), (nq + nkv + k0, nq + nkv + k1)]),
                 "o": rows(L["o"], q0, q1),
-                "gu": cols(L["gu"], [(i0, i1), (I + i0, I + i1)]),
+                "gu": cols(L["gu"], [(2 * i0, 2 * i1)]),  # interleaved: intermediate [i0, i1) is one span
                 "down": rows(L["down"], i0, i1),
             })
         return QwenWeights(layers, self.embed, self.lm_head, self.final_norm, self.hidden, i1 - i0,
@@ -398,11 +415,7 @@ class QwenDecoder:
                 self._all_reduce(b["o"])
                 kernels.rmsnorm_residual(b["o"], res, L["post_norm"], self.eps, out=(b["normed"], res_next))
             res, res_next = res_next, res
-            self._lin(b["normed"], L["gu"], b["gu"])
-            gu = b["gu"]
-            _lib.check(lib.tf_swiglu_strided(
-                gu.data_ptr(), gu.data_ptr() + self.I * gu.element_size(), b["act"].data_ptr(), self.B, self.I,
-                gu.stride(0), gu.stride(0), b["act"].stride(0), self._dt, st), "swiglu")
+            self._gate_up(b["normed"], L["gu"], b["act"])
             self._lin(b["act"], L["down"], b["mlp"])
             if not self.fused_allreduce:
                 self._all_reduce(b["mlp"])
@@ -433,9 +446,24 @@ class QwenDecoder:
         tok = best_of_ranks(b["all_best"])
         self.tokens.copy_(tok)
 
+    def _gate_up(self, x: torch.Tensor, ql: QuantLinear, act: torch.Tensor) -> None:
+        """act = silu(x @ Wg) * (x @ Wu): one fused decode kernel for up to 32
+        rows (tf_qlinear_swiglu), else the projection and a SwiGLU launch."""
+        m, k = x.shape
+        if m <= 32:
+            ws = _lib.workspaces.get(self.dev, 256)
+            _lib.check(self._lib.tf_qlinear_swiglu(
+                x.data_ptr(), x.stride(0), self._dt, ql.packed.data_ptr(), ql.scales.data_ptr(), ql.zeros.data_ptr(),
+                _lib.dtype_code(ql.scales.dtype), act.data_ptr(), act.stride(0), m, ql.packed.shape[1], k,
+                ql.packed.shape[0] * 2, ql.group_size, ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)),
+                "qlinear_swiglu")
+            return
+        gu = self._lin(x, ql, self.buf["gu"]).view(m, -1, 2, 64)
+        kernels.swiglu(gu[:, :, 0], gu[:, :, 1], out=act.view(m, -1, 64))
+
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step."""
-        return 9 * len(self.layers) + 1
+        return (8 if self.B <= 32 else 9) * len(self.layers) + 1
 
     @torch.no_grad()
     def capture(self) -> None:

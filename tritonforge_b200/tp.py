@@ -121,3 +121,13 @@ def best_of_ranks(all_best: torch.Tensor) -> torch.Tensor:
     smallest, so the result equals torch.argmax over the whole vocabulary."""
     win = torch.argmax(all_best[:, :, 0], dim=0)
     return torch.gather(all_best[:, :, 1], 0, win.unsqueeze(0)).squeeze(0)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """Columns of gate [R, I] and up [R, I] interleaved per `block` columns:
+    [gate 0:64 | up 0:64 | gate 64:128 | up 64:128 | ...] (the layout the fused
+    gate|up + SwiGLU decode kernel reads, one 128-column block per CTA)."""
+    r, i = gate.shape
+    if up.shape != gate.shape or i % block:
+        raise ValueError("gate and up must have the same shape with a multiple of the block of columns")
+    return torch.stack([gate.reshape(r, i // block, block), up.reshape(r, i // block, block)], dim=2).reshape(r, 2 * i)
