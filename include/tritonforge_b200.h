@@ -176,6 +176,15 @@ int tf_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         const int* len, int64_t B, int32_t hq, int32_t hkv, int32_t head_dim,
                         int64_t t_max, float scale, int dtype, void* stream);
 
+/* tf_decode_attention_rope: tf_rope_kv_append and tf_decode_attention in one
+ * launch (same results bit for bit): q and the new key are rotated from the
+ * q|k|v projection rows qkv [B, ld_qkv] at position pos[0], the key and value
+ * are appended to the caches at pos[0], and attention runs over pos[1]
+ * (= pos[0] + 1) cached positions. */
+int tf_decode_attention_rope(const void* qkv, int64_t ld_qkv, const void* cos_table, const void* sin_table,
+                             void* k_cache, void* v_cache, const int* pos, void* out, int64_t B, int32_t hq,
+                             int32_t hkv, int32_t head_dim, int64_t t_max, float scale, int dtype, void* stream);
+
 /* tf_swiglu_strided: SwiGLU over row-strided gate/up views (e.g. the two
  * halves of a fused gate|up projection), same math as tf_swiglu. */
 int tf_swiglu_strided(const void* gate, const void* up, void* out, int64_t M, int64_t N, int64_t ldg,

@@ -94,3 +94,39 @@ def test_swiglu_strided_halves():
     _lib.check(rc, "swiglu_strided")
     ref = oops.swiglu(f32(gu[:, :4864]), f32(gu[:, 4864:]), "float16")
     assert_rms_close(out, ref, torch.float16, "swiglu strided", max_mismatch=0.01)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("b,hq,hkv,d,t_max,pos", [(8, 14, 2, 64, 200, 137), (2, 28, 4, 128, 2304, 2048),
+                                                   (3, 64, 8, 128, 4352, 0), (1, 8, 1, 128, 600, 599),
+                                                   (32, 16, 2, 128, 1100, 515)])
+def test_fused_rope_attention_equals_separate(b, hq, hkv, d, t_max, pos, dtype):
+    """tf_decode_attention_rope == tf_rope_kv_append then tf_decode_attention, bit for bit."""
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2RotaryEmbedding
+
+    from tritonforge_b200.decode import QwenShape, hf_config
+
+    rot = Qwen2RotaryEmbedding(hf_config(QwenShape(hq * d, 128, 1, hq, hkv, d, 16))).cuda()
+    cos, sin = rot(torch.zeros(1, 1, 8, device="cuda", dtype=dtype), torch.arange(t_max, device="cuda")[None])
+    cos, sin = cos[0].contiguous(), sin[0].contiguous()
+    g = torch.Generator(device="cuda").manual_seed(b * 7 + pos)
+    qkv = torch.randn(b, (hq + 2 * hkv) * d, device="cuda", generator=g).to(dtype)
+    kc = torch.randn(b, hkv, t_max, d, device="cuda", generator=g).to(dtype)
+    vc = torch.randn(b, hkv, t_max, d, device="cuda", generator=g).to(dtype)
+    kc2, vc2 = kc.clone(), vc.clone()
+    posb = torch.tensor([pos, pos + 1], dtype=torch.int32, device="cuda")
+    lib, st, dt = _lib.load(), _lib.stream_ptr(qkv.device), _lib.dtype_code(dtype)
+    q = torch.empty(b, hq, d, device="cuda", dtype=dtype)
+    out_ref = torch.empty(b, hq * d, device="cuda", dtype=dtype)
+    _lib.check(lib.tf_rope_kv_append(qkv.data_ptr(), qkv.stride(0), q.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                     kc.data_ptr(), vc.data_ptr(), posb.data_ptr(), b, hq, hkv, d, t_max, dt, st),
+               "rope_kv_append")
+    _lib.check(lib.tf_decode_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out_ref.data_ptr(),
+                                       posb.data_ptr() + 4, b, hq, hkv, d, t_max, d ** -0.5, dt, st), "attention")
+    out = torch.empty_like(out_ref)
+    _lib.check(lib.tf_decode_attention_rope(qkv.data_ptr(), qkv.stride(0), cos.data_ptr(), sin.data_ptr(),
+                                            kc2.data_ptr(), vc2.data_ptr(), posb.data_ptr(), out.data_ptr(), b, hq,
+                                            hkv, d, t_max, d ** -0.5, dt, st), "attention_rope")
+    torch.cuda.synchronize()
+    assert torch.equal(kc2, kc) and torch.equal(vc2, vc), "the same key and value appended"
+    assert torch.equal(out, out_ref), "the same attention output"

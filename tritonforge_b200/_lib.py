@@ -53,6 +53,8 @@ SIGNATURES = {
     "tf_rope_kv_append": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32,
                                  _vp]),
     "tf_decode_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _f32, _i32, _vp]),
+    "tf_decode_attention_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _f32,
+                                        _i32, _vp]),
     "tf_swiglu_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "tf_qlinear_swiglu": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                  _vp, _sz, _vp]),

@@ -121,11 +121,34 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* r) {
                : "memory");
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
-                                                          const T* __restrict__ v_cache, T* __restrict__ out,
+// RoPE + KV append fused into the attention launch (kRope): q and the new
+// key are rotated from the q|k|v projection row with rope_append_kernel's
+// formula, and the CTA whose chunk holds the new position writes its key and
+// value into the cache before reading it.
+// 8 elements of a 16-bit type in one 16-byte register quad
+template <typename T>
+struct V8 {
+  uint4 raw;
+  __device__ __forceinline__ float get(int i) const { return Num<T>::to_f(reinterpret_cast<const T*>(&raw)[i]); }
+  __device__ __forceinline__ void set(int i, float v) { reinterpret_cast<T*>(&raw)[i] = Num<T>::from_f(v); }
+};
+
+template <typename T>
+struct RopeIn {
+  const T* qkv;
+  int64_t ld_qkv;
+  const T* cos_t;
+  const T* sin_t;
+  const int* pos_ptr;  // [position, length]
+  T* k_cache;          // the caches again, writable (the appended position)
+  T* v_cache;
+};
+
+template <typename T, int D, bool kRope>
+__global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ q, const T* k_cache,
+                                                          const T* v_cache, T* __restrict__ out,
                                                           const int* __restrict__ len_ptr, int hq, int hkv,
-                                                          int t_max, int chunk, float scale) {
+                                                          int t_max, int chunk, float scale, const RopeIn<T> rope) {
   constexpr int kWarps = 4, kThreads = 32 * kWarps;
   constexpr int kSteps = D / 16;       // k-steps of S = Q K^T
   constexpr int kWords = D / 8;        // 32-bit words of a thread's K / Q slice (D/4 elements)
@@ -157,19 +180,75 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ 
 
   const T* kb = k_cache + ((int64_t)b * hkv + kh) * t_max * D;
   const T* vb = v_cache + ((int64_t)b * hkv + kh) * t_max * D;
+  T* qrot = reinterpret_cast<T*>(o_w);  // [G][D] rotated q (kRope), before o_w is used
+  if constexpr (kRope) {
+    const int pos = *rope.pos_ptr;
+    if (pos >= 0 && pos < t_max) {
+      const T* row = rope.qkv + (int64_t)b * rope.ld_qkv;
+      const T* cr = rope.cos_t + (int64_t)pos * D;
+      const T* sr = rope.sin_t + (int64_t)pos * D;
+      const bool owner = pos >= t_begin && pos < t_begin + chunk;  // this CTA's chunk holds the new position
+      // work item: 8 consecutive rotary pairs (d, d + D/2) of one head, 16-byte loads
+      constexpr int kGroups = D / 16;
+      const int items = (g_count + (owner ? 1 : 0)) * kGroups;
+      for (int i = tid; i < items; i += kThreads) {
+        const int hh = i / kGroups, d0 = 8 * (i % kGroups);
+        const bool is_k = hh == g_count;
+        const T* src = row + (is_k ? (int64_t)(hq + kh) * D : (int64_t)(kh * g_count + hh) * D);
+        V8<T> x1, x2, c1, c2, s1, s2, o1, o2;
+        x1.raw = *reinterpret_cast<const uint4*>(src + d0);
+        x2.raw = *reinterpret_cast<const uint4*>(src + d0 + D / 2);
+        c1.raw = *reinterpret_cast<const uint4*>(cr + d0);
+        c2.raw = *reinterpret_cast<const uint4*>(cr + d0 + D / 2);
+        s1.raw = *reinterpret_cast<const uint4*>(sr + d0);
+        s2.raw = *reinterpret_cast<const uint4*>(sr + d0 + D / 2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o1.set(e, round_to<T>(x1.get(e) * c1.get(e)) + round_to<T>(-x2.get(e) * s1.get(e)));
+          o2.set(e, round_to<T>(x2.get(e) * c2.get(e)) + round_to<T>(x1.get(e) * s2.get(e)));
+        }
+        if (is_k) {
+          T* kd = rope.k_cache + (((int64_t)b * hkv + kh) * t_max + pos) * D;
+          T* vd = rope.v_cache + (((int64_t)b * hkv + kh) * t_max + pos) * D;
+          const T* vs = row + (int64_t)(hq + hkv + kh) * D;
+          *reinterpret_cast<uint4*>(kd + d0) = o1.raw;
+          *reinterpret_cast<uint4*>(kd + d0 + D / 2) = o2.raw;
+          *reinterpret_cast<uint4*>(vd + d0) = *reinterpret_cast<const uint4*>(vs + d0);
+          *reinterpret_cast<uint4*>(vd + d0 + D / 2) = *reinterpret_cast<const uint4*>(vs + d0 + D / 2);
+        } else {
+          *reinterpret_cast<uint4*>(qrot + hh * D + d0) = o1.raw;
+          *reinterpret_cast<uint4*>(qrot + hh * D + d0 + D / 2) = o2.raw;
+        }
+      }
+      if (owner) __threadfence();  // the appended key/value reach L2 before this CTA's copies read them
+    } else {
+      for (int i = tid; i < g_count * D; i += kThreads) qrot[i] = Num<T>::from_f(0.f);
+    }
+    __syncthreads();
+  }
   // Q fragment: head g of this kv head, elements [qd*D/4, (qd+1)*D/4)
   uint32_t qf[kWords];
   if (g < g_count) {
-    const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)b * hq + (int64_t)kh * g_count + g) * D + qd * (D / 4));
+    if constexpr (kRope) {
+      const uint4* qs = reinterpret_cast<const uint4*>(qrot + g * D + qd * (D / 4));
 #pragma unroll
-    for (int c = 0; c < kWords / 4; ++c) {
-      const uint4 v = __ldg(qs + c);
-      qf[4 * c] = v.x; qf[4 * c + 1] = v.y; qf[4 * c + 2] = v.z; qf[4 * c + 3] = v.w;
+      for (int c = 0; c < kWords / 4; ++c) {
+        const uint4 v = qs[c];
+        qf[4 * c] = v.x; qf[4 * c + 1] = v.y; qf[4 * c + 2] = v.z; qf[4 * c + 3] = v.w;
+      }
+    } else {
+      const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)b * hq + (int64_t)kh * g_count + g) * D + qd * (D / 4));
+#pragma unroll
+      for (int c = 0; c < kWords / 4; ++c) {
+        const uint4 v = __ldg(qs + c);
+        qf[4 * c] = v.x; qf[4 * c + 1] = v.y; qf[4 * c + 2] = v.z; qf[4 * c + 3] = v.w;
+      }
     }
   } else {
 #pragma unroll
     for (int c = 0; c < kWords; ++c) qf[c] = 0u;
   }
+  if constexpr (kRope) __syncthreads();  // qrot (in o_w) is read before any warp merges into o_w
 
   float o_acc[kNT][4];
 #pragma unroll
@@ -187,7 +266,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const T* __restrict__ 
       const uint4* ks = reinterpret_cast<const uint4*>(kb + (int64_t)t * D + qd * (D / 4));
 #pragma unroll
       for (int c = 0; c < kWords / 4; ++c) {
-        const uint4 v = __ldg(ks + c);
+        const uint4 v = ks[c];  // cached load (not the read-only path): sees a key this CTA appended
         kf[h][4 * c] = v.x; kf[h][4 * c + 1] = v.y; kf[h][4 * c + 2] = v.z; kf[h][4 * c + 3] = v.w;
       }
     }
@@ -397,18 +476,14 @@ size_t decode_attention_smem(int head_dim) {
 }  // namespace
 }  // namespace tf
 
-extern "C" int tf_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
-                                   const int* len, int64_t B, int32_t hq, int32_t hkv, int32_t head_dim,
-                                   int64_t t_max, float scale, int dtype, void* stream) {
-  using namespace tf;
-  if (B < 0 || hq <= 0 || hkv <= 0 || hq % hkv || t_max <= 0) return fail(TF_ERR_BAD_SHAPE, "decode_attention: bad shape");
-  if (head_dim != 64 && head_dim != 128) return fail(TF_ERR_UNSUPPORTED, "decode_attention: head_dim %d", head_dim);
+namespace tf {
+namespace {
+template <typename T, bool kRope>
+int launch_attention(const void* q, const void* k_cache, const void* v_cache, void* out, const int* len, int64_t B,
+                     int hq, int hkv, int head_dim, int64_t t_max, float scale, const RopeIn<T>& rope,
+                     cudaStream_t st) {
   const int g = hq / hkv;
-  if (g > 8) return fail(TF_ERR_UNSUPPORTED, "decode_attention: %d q heads per kv head (max 8)", g);
-  if (B == 0) return TF_OK;
-  if (B > 65535) return fail(TF_ERR_BAD_SHAPE, "decode_attention: batch too large");
-  if (!q || !k_cache || !v_cache || !out || !len) return fail(TF_ERR_BAD_ARG, "decode_attention: null pointer");
-  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(TF_ERR_UNALIGNED, "decode_attention: caches must be 16-byte aligned");
+  (void)g;
   // split the context over a cluster: >= 2 CTAs per SM when the batch is
   // small, and chunks of at most 512 positions (up to 8 splits) so that long
   // contexts keep several CTAs resident per SM
@@ -423,22 +498,69 @@ extern "C" int tf_decode_attention(const void* q, const void* k_cache, const voi
   const int chunk = (int)cdiv(t_max, splits);
   const size_t smem = decode_attention_smem(head_dim);
   const dim3 grid((unsigned)hkv, (unsigned)B, (unsigned)splits), cluster(1, 1, (unsigned)splits);
+  auto go = [&](auto kern) -> int {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return launch_ex("decode_attention", kern, grid, dim3(128), smem, st, cluster, (const T*)q, (const T*)k_cache,
+                     (const T*)v_cache, (T*)out, len, hq, hkv, (int)t_max, chunk, scale, rope);
+  };
+  if (head_dim == 64) return go(decode_attn_kernel<T, 64, kRope>);
+  return go(decode_attn_kernel<T, 128, kRope>);
+}
+
+int check_attention(const void* q, const void* k_cache, const void* v_cache, void* out, const int* len, int64_t B,
+                    int hq, int hkv, int head_dim, int64_t t_max) {
+  if (B < 0 || hq <= 0 || hkv <= 0 || hq % hkv || t_max <= 0) return fail(TF_ERR_BAD_SHAPE, "decode_attention: bad shape");
+  if (head_dim != 64 && head_dim != 128) return fail(TF_ERR_UNSUPPORTED, "decode_attention: head_dim %d", head_dim);
+  if (hq / hkv > 8) return fail(TF_ERR_UNSUPPORTED, "decode_attention: %d q heads per kv head (max 8)", hq / hkv);
+  if (B > 65535) return fail(TF_ERR_BAD_SHAPE, "decode_attention: batch too large");
+  if (B > 0 && (!q || !k_cache || !v_cache || !out || !len)) return fail(TF_ERR_BAD_ARG, "decode_attention: null pointer");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(TF_ERR_UNALIGNED, "decode_attention: caches must be 16-byte aligned");
+  return TF_OK;
+}
+}  // namespace
+}  // namespace tf
+
+extern "C" int tf_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                   const int* len, int64_t B, int32_t hq, int32_t hkv, int32_t head_dim,
+                                   int64_t t_max, float scale, int dtype, void* stream) {
+  using namespace tf;
+  int rc = check_attention(q, k_cache, v_cache, out, len, B, hq, hkv, head_dim, t_max);
+  if (rc != TF_OK || B == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define TF_ATTN(T, DD)                                                                                          \
-  {                                                                                                             \
-    auto kern = decode_attn_kernel<T, DD>;                                                                      \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-    return launch_ex("decode_attention", kern, grid, dim3(128), smem, st, cluster, (const T*)q,                \
-                     (const T*)k_cache, (const T*)v_cache, (T*)out, len, (int)hq, (int)hkv, (int)t_max, chunk,  \
-                     scale);                                                                                    \
-  }
-  if (dtype == TF_F16) {
-    if (head_dim == 64) TF_ATTN(__half, 64) else TF_ATTN(__half, 128)
-  } else if (dtype == TF_BF16) {
-    if (head_dim == 64) TF_ATTN(__nv_bfloat16, 64) else TF_ATTN(__nv_bfloat16, 128)
-  }
-#undef TF_ATTN
+  if (dtype == TF_F16)
+    return launch_attention<__half, false>(q, k_cache, v_cache, out, len, B, hq, hkv, head_dim, t_max, scale,
+                                           RopeIn<__half>{}, st);
+  if (dtype == TF_BF16)
+    return launch_attention<__nv_bfloat16, false>(q, k_cache, v_cache, out, len, B, hq, hkv, head_dim, t_max, scale,
+                                                  RopeIn<__nv_bfloat16>{}, st);
   return fail(TF_ERR_BAD_DTYPE, "decode_attention: unsupported dtype %d", dtype);
+}
+
+extern "C" int tf_decode_attention_rope(const void* qkv, int64_t ld_qkv, const void* cos_table, const void* sin_table,
+                                        void* k_cache, void* v_cache, const int* pos, void* out, int64_t B,
+                                        int32_t hq, int32_t hkv, int32_t head_dim, int64_t t_max, float scale,
+                                        int dtype, void* stream) {
+  using namespace tf;
+  int rc = check_attention(qkv, k_cache, v_cache, out, pos, B, hq, hkv, head_dim, t_max);
+  if (rc != TF_OK || B == 0) return rc;
+  if (!cos_table || !sin_table) return fail(TF_ERR_BAD_ARG, "decode_attention_rope: null pointer");
+  if (ld_qkv < (int64_t)(hq + 2 * hkv) * head_dim) return fail(TF_ERR_BAD_SHAPE, "decode_attention_rope: ld_qkv too small");
+  if (ld_qkv % 8 || !aligned(qkv, 16) || !aligned(cos_table, 16) || !aligned(sin_table, 16))
+    return fail(TF_ERR_UNALIGNED, "decode_attention_rope: qkv rows and rotary tables must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_F16) {
+    RopeIn<__half> r{(const __half*)qkv, ld_qkv, (const __half*)cos_table, (const __half*)sin_table, pos,
+                     (__half*)k_cache, (__half*)v_cache};
+    return launch_attention<__half, true>(nullptr, k_cache, v_cache, out, pos + 1, B, hq, hkv, head_dim, t_max, scale,
+                                          r, st);
+  }
+  if (dtype == TF_BF16) {
+    RopeIn<__nv_bfloat16> r{(const __nv_bfloat16*)qkv, ld_qkv, (const __nv_bfloat16*)cos_table,
+                            (const __nv_bfloat16*)sin_table, pos, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache};
+    return launch_attention<__nv_bfloat16, true>(nullptr, k_cache, v_cache, out, pos + 1, B, hq, hkv, head_dim, t_max,
+                                                 scale, r, st);
+  }
+  return fail(TF_ERR_BAD_DTYPE, "decode_attention_rope: unsupported dtype %d", dtype);
 }
 
 extern "C" int tf_swiglu_strided(const void* gate, const void* up, void* out, int64_t M, int64_t N, int64_t ldg,

@@ -8,8 +8,7 @@ docs/FINAL_REPORT.md:93-99). Per layer:
 
     rmsnorm_residual(mlp_out_prev, residual)  -> normed, residual      (layer 0: rmsnorm)
     quantized_linear(normed, [q|k|v])          -> qkv                   (one GEMV, bias)
-    rope_kv_append(qkv)                        -> q rotated, K/V cache at pos
-    decode_attention(q, cache, len=pos+1)      -> attn
+    decode_attention_rope(qkv, cache, pos)     -> attn (q and the new key rotated, K/V appended at pos)
     quantized_linear(attn, o)                  -> o
     rmsnorm_residual(o, residual)              -> normed, residual
     qlinear_swiglu(normed, [gate|up])          -> act = silu(gate) * up (one GEMV, fused epilogue)
@@ -400,14 +399,10 @@ class QwenDecoder:
                     kernels.rmsnorm_residual(b["mlp"], res, L["in_norm"], self.eps, out=(b["normed"], res_next))
                 res, res_next = res_next, res
             self._lin(b["normed"], L["qkv"], b["qkv"])
-            _lib.check(lib.tf_rope_kv_append(
-                b["qkv"].data_ptr(), b["qkv"].stride(0), b["q"].data_ptr(), self.cos.data_ptr(),
-                self.sin.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), posp,
-                self.B, self.Hq, self.Hkv, self.D, self.T, self._dt, st), "rope_kv_append")
-            _lib.check(lib.tf_decode_attention(
-                b["q"].data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
-                b["attn"].data_ptr(), lenp, self.B, self.Hq, self.Hkv, self.D, self.T, self.scale,
-                self._dt, st), "decode_attention")
+            _lib.check(lib.tf_decode_attention_rope(
+                b["qkv"].data_ptr(), b["qkv"].stride(0), self.cos.data_ptr(), self.sin.data_ptr(),
+                self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), posp, b["attn"].data_ptr(), self.B,
+                self.Hq, self.Hkv, self.D, self.T, self.scale, self._dt, st), "decode_attention_rope")
             self._lin(b["attn"], L["o"], b["o"])
             if self.fused_allreduce:
                 self._ar_norm("o", res, L["post_norm"], b["normed"], res_next)
@@ -463,7 +458,7 @@ class QwenDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step."""
-        return (8 if self.B <= 32 else 9) * len(self.layers) + 1
+        return (7 if self.B <= 32 else 8) * len(self.layers) + 1
 
     @torch.no_grad()
     def capture(self) -> None:
