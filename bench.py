@@ -299,10 +299,10 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
 
     def run():
         for x, ql, out in launches:
-            if ql is not None and out is b["act"]:
+            if out is b["act"]:
                 dec._gate_up(x, ql, out)  # fused gate|up + SwiGLU (the step's own launch)
             else:
-                kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
+                dec._lin(x, ql, out)
 
     s = torch.cuda.Stream(dec.dev)
     with torch.cuda.stream(s):
@@ -323,14 +323,18 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
     torch.cuda.synchronize(dec.dev)
     total_us = e0.elapsed_time(e1) * 1e3 / reps
     alg = 0
+    kinds = set()
     for x, ql, out in launches:
         m, k = x.shape
-        kp, n = ql.packed.shape[0] * 2, ql.packed.shape[1]
+        kp, n = ql.scales.shape[0] * ql.group_size, ql.scales.shape[1]
+        kinds.add(type(ql).__name__)
         alg += m * k * 2 + kp * n // 2 + 2 * (kp // ql.group_size) * n * 2 + out.numel() * out.element_size()
         if ql.bias is not None:
             alg += n * 2
     achieved = alg / (total_us * 1e-6) / 1e9
-    return {"kernel": "gemv_int4 (tf_qlinear decode regime)", "bound": "hbm", "achieved": achieved,
+    kernel = " + ".join(sorted({"CMLinear": "gemv_int4_cm (tcgen05, tiled column-major weights)",
+                                "QuantLinear": "gemv_int4 (mma.sync, K-major weights)"}[k] for k in kinds))
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved,
             "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs, "traffic": None,
             "launches_per_step": len(launches), "algorithmic_bytes_per_step": alg,
             "us_per_launch": total_us / len(launches)}
@@ -354,10 +358,13 @@ def run_ours(args) -> None:
         args.want_cpu = False
         weights = QwenWeights.synthetic(args.model, tp=world, rank=rank, dtype=torch.bfloat16, device=dev,
                                         seed=0)
+        lo, hi = QwenDecoder.COLMAJOR_BATCH
+        if args.layout == "cm" or (args.layout == "auto" and lo <= args.batch <= hi):
+            weights.to_colmajor()  # in place: one copy of the weights in HBM
         max_len = args.prompt + args.warmup + 2 * args.steps + 8
         group = dist.group.WORLD if world > 1 else None
         dec = QwenDecoder(weights, batch=args.batch, max_len=max_len, group=group,
-                          fused_allreduce=args.allreduce == "fused")
+                          fused_allreduce=args.allreduce == "fused", colmajor=args.layout == "cm")
         dec.fill_cache(args.prompt, seed=1)
     else:
         args.want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
@@ -365,7 +372,8 @@ def run_ours(args) -> None:
         vocab = model.config.vocab_size
         prompt = prompt_ids(args, vocab, rank)
         max_len = args.prompt + args.warmup + 2 * args.steps + 8
-        dec = QwenDecoder(model, batch=args.batch, max_len=max_len)
+        dec = QwenDecoder(model, batch=args.batch, max_len=max_len,
+                          colmajor={"auto": None, "cm": True, "kmajor": False}[args.layout])
         # prefill in chunks of M <= 32 rows so every projection runs the decode kernel
         dec.prefill(prompt, chunk=max(1, 32 // args.batch))
     dec.capture()
@@ -421,8 +429,12 @@ def run_ours(args) -> None:
     roof["peak_source"] = peaks["source"]
     # DRAM traffic: an ncu capture of one GEMV launch (read + write bytes over
     # its algorithmic bytes, committed under profiles/), scaled to the step
+    traffic_file = {"gemv_int4 (mma.sync, K-major weights)": "gemv_dram_traffic.json",
+                    "gemv_int4_cm (tcgen05, tiled column-major weights)": "gemv_cm_dram_traffic.json"}.get(roof["kernel"])
     try:
-        with open(os.path.join(ROOT, "profiles", "gemv_dram_traffic.json")) as f:
+        if traffic_file is None:
+            raise OSError("projections of both layouts")
+        with open(os.path.join(ROOT, "profiles", traffic_file)) as f:
             tr = json.load(f)
         roof["traffic"] = tr["ratio"] * roof["algorithmic_bytes_per_step"]
         roof["traffic_unit"] = "bytes per step"
@@ -481,6 +493,9 @@ def main() -> None:
                     help="tensor parallel: fused all-reduce + RMSNorm over peer memory, or NCCL + RMSNorm")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layout", choices=["auto", "cm", "kmajor"], default="auto",
+                    help="int4 weight layout of the decode projections: tiled column-major (tcgen05 kernel), "
+                         "the reference's K-major (mma.sync kernel), or auto (column-major for batches 9..64)")
     args = ap.parse_args()
     if args.batch is None:
         args.batch = 8 if args.model == "0.5b" else 32

@@ -201,6 +201,44 @@ int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* pa
                       const void* zeros, int param_dtype, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
                       int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tf_repack_int4_cm: the reference's packed int4 weights [K_pad/2, N]
+ * (K-major, low nibble = even k; reference src/tritonforge/quant.py:25-63)
+ * -> the tiled column-major layout of the decode kernels: 16 KiB tiles
+ * [ceil(N/256)][K_pad/128][256 columns][64 B]. In a tile row (one output
+ * column, 128 k) 32-bit word w holds k = 8w..8w+7 with nibble p = k 8w+2p and
+ * nibble p+4 = k 8w+2p+1 (p = 0..3), and 16-byte chunk c is stored at position
+ * c ^ ((row / 2) & 3). Columns >= N are zero. Same codes, another order: a
+ * decode engine converts its weights once (no reference counterpart).
+ * K_pad % 128 == 0; packed_cm holds tf_int4_cm_bytes(N, K_pad) bytes and is
+ * 16-byte aligned. */
+size_t tf_int4_cm_bytes(int64_t N, int64_t K_pad);
+int tf_repack_int4_cm(const uint8_t* packed, uint8_t* packed_cm, int64_t N, int64_t K_pad, void* stream);
+
+/* tf_qlinear_cm: tf_qlinear on tiled column-major weights (tf_repack_int4_cm),
+ * decode regime: 1 <= M <= 64, x and scales/zeros of the same 16-bit type,
+ * K % 64 == 0, group_size % 128 == 0, N % 16 == 0, 16-byte aligned operands.
+ * Same outputs as tf_qlinear within the floating-point contract (weights
+ * dequantised bit-exactly, fp32 accumulation, the same roundings); computed
+ * on the tcgen05 tensor cores (weights on the MMA's N = 256). Replaces
+ * quantized_linear (reference src/tritonforge/kernels/dequant_gemm.py:121-210)
+ * inside the decode engine. Long k ranges are split over a thread-block
+ * cluster whose CTAs add their partial tiles through distributed shared
+ * memory in rank order (results do not depend on timing). `workspace` holds
+ * tf_qlinear_cm_workspace_bytes(M, N, K_pad) bytes (the error word of the
+ * bounded waits), zeroed before its first use. */
+size_t tf_qlinear_cm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
+int tf_qlinear_cm(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm, const void* scales,
+                  const void* zeros, int param_dtype, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                  int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* tf_qlinear_cm_swiglu: tf_qlinear_swiglu on tiled column-major weights
+ * (gate/up interleaved per 64 columns before the repack); constraints and
+ * workspace of tf_qlinear_cm, N % 128 == 0. */
+int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm, const void* scales,
+                         const void* zeros, int param_dtype, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                         int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+
 /* tf_allreduce_rmsnorm_residual: tensor-parallel all-reduce of row-parallel
  * partial sums fused with residual-add + RMSNorm (no reference counterpart:
  * the reference is single-GPU; it replaces an all-reduce followed by

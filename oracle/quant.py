@@ -6,6 +6,8 @@ Follows ``src/tritonforge/quant.py`` of the reference:
 * ``quantize_int4_group``    -> quant.py:29-63
 * ``unpack_int4``            -> quant.py:66-74
 * ``dequantize_int4``        -> quant.py:77-105 (``_group_expand`` + dequant)
+* ``repack_cm`` / ``unpack_cm`` -> the decode engine's tiled column-major layout of
+  the same codes (no reference counterpart)
 
 Format (the drop-in contract): for a weight ``W[N, K]`` (``nn.Linear`` layout)
 K is zero-padded to ``K_pad`` (a multiple of the group size ``g``). Per
@@ -123,6 +125,58 @@ def unpack_int4(packed: np.ndarray, k: int | None = None) -> np.ndarray:
     out[0::2] = packed & 0x0F
     out[1::2] = (packed >> 4) & 0x0F
     return out if k is None else out[:k]
+
+
+CM_COLS = 256  # columns of a tile of the tiled column-major layout
+CM_K = 128     # k of a tile
+
+
+def repack_cm(packed: np.ndarray) -> np.ndarray:
+    """Tiled column-major layout used by the decode engine (a layout of the
+    same codes, no reference counterpart): packed [K_pad/2, N] -> uint8
+    [ceil(N/256), K_pad/128, 256, 64]. Tile (b, s) row r is column 256 b + r,
+    k = 128 s .. 128 s + 127: little-endian 32-bit word w holds k = 8w..8w+7 of
+    the tile with nibble p = code[8w + 2p] and nibble p + 4 = code[8w + 2p + 1]
+    (p = 0..3); 16-byte chunk c of the row is stored at c ^ ((r // 2) % 4).
+    Columns >= N are zero."""
+    codes = unpack_int4(packed).astype(np.uint32)  # [K_pad, N]
+    kp, n = codes.shape
+    if kp % CM_K:
+        raise ValueError("K_pad must be a multiple of 128")
+    nb = -(-n // CM_COLS)
+    full = np.zeros((kp, nb * CM_COLS), np.uint32)
+    full[:, :n] = codes
+    c = full.T.reshape(nb, CM_COLS, kp // CM_K, 16, 8)  # [block, row, stage, word, k in word]
+    words = np.zeros(c.shape[:4], np.uint32)
+    for p in range(4):
+        words |= c[..., 2 * p] << (4 * p)
+        words |= c[..., 2 * p + 1] << (4 * p + 16)
+    words = words.transpose(0, 2, 1, 3)  # [block, stage, row, word]
+    chunks = words.reshape(nb, kp // CM_K, CM_COLS, 4, 4)  # 16-byte chunks of 4 words
+    out = np.empty_like(chunks)
+    rows = np.arange(CM_COLS)
+    for ch in range(4):
+        out[:, :, rows, ch ^ ((rows // 2) % 4)] = chunks[:, :, rows, ch]
+    return out.astype("<u4").view(np.uint8).reshape(nb, kp // CM_K, CM_COLS, 64)
+
+
+def unpack_cm(tiles: np.ndarray, n: int) -> np.ndarray:
+    """Inverse of ``repack_cm``: tiles [NB, S, 256, 64] -> codes [K_pad, n]."""
+    t = np.ascontiguousarray(tiles, dtype=np.uint8)
+    nb, ns = t.shape[:2]
+    chunks = t.view("<u4").reshape(nb, ns, CM_COLS, 4, 4).astype(np.uint32)
+    rows = np.arange(CM_COLS)
+    logical = np.empty_like(chunks)
+    for ch in range(4):
+        logical[:, :, rows, ch] = chunks[:, :, rows, ch ^ ((rows // 2) % 4)]
+    words = logical.reshape(nb, ns, CM_COLS, 16)
+    codes = np.empty((nb, ns, CM_COLS, 16, 8), np.uint8)
+    for p in range(4):
+        codes[..., 2 * p] = (words >> (4 * p)) & 15
+        codes[..., 2 * p + 1] = (words >> (4 * p + 16)) & 15
+    # [block, stage, row, k in stage] -> [k, column]
+    k_major = codes.reshape(nb, ns, CM_COLS, CM_K).transpose(1, 3, 0, 2).reshape(ns * CM_K, nb * CM_COLS)
+    return k_major[:, :n].copy()
 
 
 def dequantize_int4_f32(packed, scales_f32, zeros_f32, group_size: int = 128) -> np.ndarray:

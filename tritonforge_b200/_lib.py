@@ -58,6 +58,13 @@ SIGNATURES = {
     "tf_swiglu_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "tf_qlinear_swiglu": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                  _vp, _sz, _vp]),
+    "tf_int4_cm_bytes": (_sz, [_i64, _i64]),
+    "tf_repack_int4_cm": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "tf_qlinear_cm_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "tf_qlinear_cm": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
+                             _i64, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
+    "tf_qlinear_cm_swiglu": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
+                                    _vp, _sz, _vp]),
     "tf_allreduce_rmsnorm_residual": (_i32, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp,
                                              _i64, _i64, _f32, _i32, _vp, _vp]),
 }
@@ -130,25 +137,28 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 class _Workspaces:
-    """Per-device zero-initialised scratch handed to the kernels (its header
-    holds the device error word of the bounded waits; the kernels keep no other
-    state in it).
+    """Zero-initialised scratch handed to the kernels, one buffer per (device,
+    stream): its header holds the device error word of the bounded waits, and
+    the column-major decode kernel keeps the arrival counters and partial
+    tiles of split column blocks after it (left zeroed by every call). Calls
+    that share a buffer are therefore ordered on their stream.
 
     A buffer is zeroed only when it is (re)allocated. Reallocation happens
     outside any CUDA-graph capture: callers that capture size it first with
-    ``reserve``.
+    ``reserve`` (or run the captured work once on the capture stream).
     """
 
     def __init__(self) -> None:
-        self._bufs: dict[int, torch.Tensor] = {}
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
 
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
         idx = device.index if device.index is not None else torch.cuda.current_device()
-        buf = self._bufs.get(idx)
+        key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+        buf = self._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
             size = max(nbytes, 1 << 20, 0 if buf is None else 2 * buf.numel())
             buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
-            self._bufs[idx] = buf
+            self._bufs[key] = buf
         return buf
 
     def reserve(self, device: torch.device, nbytes: int) -> None:

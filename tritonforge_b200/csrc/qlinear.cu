@@ -108,3 +108,41 @@ extern "C" int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const 
   if (!gemv_supported(pb)) return fail(TF_ERR_UNSUPPORTED, "qlinear_swiglu: needs the decode regime (M <= 32)");
   return gemv_launch(pb, static_cast<cudaStream_t>(stream), true);
 }
+
+extern "C" size_t tf_qlinear_cm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad) {
+  return tf::gemv_cm_workspace_bytes(M, N, K_pad);
+}
+
+extern "C" int tf_qlinear_cm(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm, const void* scales,
+                             const void* zeros, int param_dtype, const void* bias, int bias_dtype, void* out,
+                             int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,         x_dtype, packed_cm, scales,    zeros,          param_dtype,
+                    bias, bias_dtype,  out,     ldo,       M,         N,              K,
+                    K_pad, group_size, workspace, workspace_bytes};
+  int rc = validate(pb);
+  if (rc != TF_OK || M == 0 || N == 0) return rc;
+  if (!gemv_cm_supported(pb))
+    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
+  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm,
+                                    const void* scales, const void* zeros, int param_dtype, void* out, int64_t ldo,
+                                    int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,     x_dtype, packed_cm, scales, zeros, param_dtype, nullptr, 0, out, ldo,
+                    M,    N,       K,       K_pad,     group_size, workspace, workspace_bytes};
+  pb.ldo = ldo >= N ? ldo : N;
+  int rc = validate(pb);
+  if (rc != TF_OK) return rc;
+  if (ldo < N / 2) return fail(TF_ERR_BAD_SHAPE, "qlinear_cm_swiglu: ldo %lld < N/2", (long long)ldo);
+  if (M == 0 || N == 0) return TF_OK;
+  pb.ldo = ldo;
+  if (N % 128 != 0) return fail(TF_ERR_BAD_SHAPE, "qlinear_cm_swiglu: N=%lld not a multiple of 128", (long long)N);
+  if (!gemv_cm_supported(pb))
+    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm_swiglu: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
+  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream), true);
+}

@@ -33,6 +33,12 @@ size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
 // kernel stores round(silu(g) * u) [M, N/2] instead of the projections
 int gemv_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = false);
 
+// Column-major packed weights (packed_cm [N, K_pad/2], tf_repack_int4_cm),
+// M <= 32, x and scales of one type: tcgen05 with the weights in tensor memory
+bool gemv_cm_supported(const QLinearProblem& pb);
+size_t gemv_cm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
+int gemv_cm_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = false);
+
 bool gemm_supported(const QLinearProblem& pb);
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
 int gemm_launch(const QLinearProblem& pb, cudaStream_t st);

@@ -36,6 +36,7 @@ import dataclasses
 import torch
 
 from . import _lib, kernels
+from .colmajor import CMLinear, qlinear_cm_swiglu
 from .integration.qwen import QuantLinear
 
 
@@ -195,6 +196,34 @@ class QwenWeights:
                    lay.kv_local, D, shape.eps, shape.rope_theta)
 
 
+    LINEARS = ("qkv", "o", "gu", "down")
+
+    def colmajor_layers(self, min_k: int = 2048) -> list:
+        """The layers with every projection whose input width is at least
+        `min_k` in the tiled column-major layout (CMLinear, the tcgen05 decode
+        kernel, faster from 9 rows up on wide layers); narrower ones stay
+        K-major (the mma.sync kernel wins where a column block has few k
+        stages). New layer dicts; the original tensors are not touched."""
+        from .colmajor import CMLinear
+
+        out = []
+        for L in self.layers:
+            d = dict(L)
+            for name in self.LINEARS:
+                ql = L[name]
+                if isinstance(ql, QuantLinear) and ql.packed.shape[0] * 2 >= min_k:
+                    d[name] = CMLinear.from_quant(ql)
+            out.append(d)
+        return out
+
+    def to_colmajor(self, min_k: int = 2048) -> "QwenWeights":
+        """`colmajor_layers` in place: the K-major packed tensors are dropped
+        (memory for one copy of the weights). Shard before converting."""
+        for i, d in enumerate(self.colmajor_layers(min_k)):
+            self.layers[i] = d
+        torch.cuda.empty_cache()
+        return self
+
     def shard(self, tp: int, rank: int) -> "QwenWeights":
         """This rank's tensor-parallel shard of full (tp=1) weights: slices of
         the quantised tensors, bit-identical to quantising the shard alone."""
@@ -256,8 +285,11 @@ class QwenDecoder:
     `group` is a torch.distributed process group, or any object with an
     `all_reduce(tensor)` method that sums in place across the ranks."""
 
+    # batches the tcgen05 decode kernel (tiled column-major weights) serves
+    COLMAJOR_BATCH = (9, 64)
+
     def __init__(self, model_or_weights, batch: int, max_len: int, group=None, vocab_parallel: bool | None = None,
-                 fused_allreduce: bool | None = None):
+                 fused_allreduce: bool | None = None, colmajor: bool | None = None):
         w = model_or_weights if isinstance(model_or_weights, QwenWeights) else QwenWeights.from_hf(model_or_weights)
         self.w = w
         self.model = w.model
@@ -278,7 +310,16 @@ class QwenDecoder:
         self.H, self.I = w.hidden, w.inter
         self.Hq, self.Hkv, self.D = w.q_heads, w.kv_heads, w.head_dim
         self.eps = w.eps
-        self.layers = w.layers
+        # Weight layout: projections already converted (QwenWeights.to_colmajor)
+        # are used as they are; otherwise, for batches the tcgen05 decode kernel
+        # serves (colmajor=None) or when asked, this decoder converts its own
+        # copies of the wide projections.
+        lo, hi = self.COLMAJOR_BATCH
+        if colmajor is None:
+            colmajor = lo <= batch <= hi
+        if batch > hi and (colmajor or any(isinstance(L[n], CMLinear) for L in w.layers for n in w.LINEARS)):
+            raise ValueError(f"column-major weights serve batches up to {hi} (got {batch})")
+        self.layers = w.colmajor_layers() if colmajor else w.layers
         self.final_norm, self.embed, self.lm_head = w.final_norm, w.embed, w.lm_head
         self.vocab = w.lm_head.shape[0]
         self.v0 = 0
@@ -365,7 +406,9 @@ class QwenDecoder:
         return int(self._ar_err.item()) if self.fused_allreduce else 0
 
     # ------------------------------------------------------------------ step
-    def _lin(self, x: torch.Tensor, ql: QuantLinear, out: torch.Tensor) -> torch.Tensor:
+    def _lin(self, x: torch.Tensor, ql, out: torch.Tensor) -> torch.Tensor:
+        if isinstance(ql, CMLinear):
+            return ql(x, out=out)
         return kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
 
     def _all_reduce(self, t: torch.Tensor) -> None:
@@ -441,11 +484,15 @@ class QwenDecoder:
         tok = best_of_ranks(b["all_best"])
         self.tokens.copy_(tok)
 
-    def _gate_up(self, x: torch.Tensor, ql: QuantLinear, act: torch.Tensor) -> None:
+    def _gate_up(self, x: torch.Tensor, ql, act: torch.Tensor) -> None:
         """act = silu(x @ Wg) * (x @ Wu): one fused decode kernel for up to 32
-        rows (tf_qlinear_swiglu), else the projection and a SwiGLU launch."""
+        rows (tf_qlinear_swiglu; up to 64 with column-major weights,
+        tf_qlinear_cm_swiglu), else the projection and a SwiGLU launch."""
         m, k = x.shape
-        if m <= 32:
+        if isinstance(ql, CMLinear) and m <= 64:
+            qlinear_cm_swiglu(x, ql.tiles, ql.scales, ql.zeros, ql.group_size, out=act)
+            return
+        if isinstance(ql, QuantLinear) and m <= 32:
             ws = _lib.workspaces.get(self.dev, 256)
             _lib.check(self._lib.tf_qlinear_swiglu(
                 x.data_ptr(), x.stride(0), self._dt, ql.packed.data_ptr(), ql.scales.data_ptr(), ql.zeros.data_ptr(),
@@ -458,7 +505,11 @@ class QwenDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step."""
-        return (7 if self.B <= 32 else 8) * len(self.layers) + 1
+        n = 1
+        for L in self.layers:
+            fused = self.B <= (64 if isinstance(L["gu"], CMLinear) else 32)
+            n += 7 if fused else 8
+        return n
 
     @torch.no_grad()
     def capture(self) -> None:

@@ -1,11 +1,13 @@
 """One kernel of the decode / prefill path on a bounded case, for an ncu
 capture of a single launch (the first launches are warm-up):
 
-    python -m tritonforge_b200.profile_cases gemv|attention|gemm
+    python -m tritonforge_b200.profile_cases gemv|gemv_cm|attention|gemm
 
 gemv:      int4 GEMV of the Qwen2.5-72B gate|up projection (K=8192, N=59136,
            bf16, int4 g128) at M=32 rows (the 72B decode at batch 32);
            242 MB of packed weights, larger than the 126 MB L2.
+gemv_cm:   the same projection with the weights in the tiled column-major
+           layout (tcgen05 decode kernel, tf_qlinear_cm).
 attention: decode attention of the 72B shape (64 q / 8 kv heads of 128) at
            batch 32 over a 4096-position bf16 KV cache (1.07 GB of K/V).
 gemm:      prefill-regime int4 linear of the 7B gate projection (K=3584,
@@ -16,7 +18,7 @@ import sys
 
 import torch
 
-from tritonforge_b200 import _lib, kernels, quant
+from tritonforge_b200 import _lib, colmajor, kernels, quant
 
 
 def main(case: str) -> None:
@@ -30,6 +32,17 @@ def main(case: str) -> None:
         out = torch.empty(m, n, device="cuda", dtype=dt)
         for _ in range(3):
             kernels.quantized_linear(x, p, s, z, None, 128, {"regime": case}, out=out)
+    elif case == "gemv_cm":
+        m, k, n = 32, 8192, 59136
+        w = torch.randn(n, k, device="cuda") * 0.02
+        p, s, z, _ = quant.quantize_int4_group(w, 128, dt)
+        del w
+        tiles = colmajor.repack_cm(p)
+        del p
+        x = torch.randn(m, k, device="cuda").to(dt)
+        out = torch.empty(m, n, device="cuda", dtype=dt)
+        for _ in range(3):
+            colmajor.quantized_linear_cm(x, tiles, s, z, None, 128, out=out)
     elif case == "attention":
         b, hq, hkv, d, ctx = 32, 64, 8, 128, 4096
         t_max = ctx + 64
