@@ -271,6 +271,17 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def _layout_desc(args) -> str:
+    from tritonforge_b200.decode import QwenDecoder
+
+    lo, hi = QwenDecoder.COLMAJOR_BATCH
+    cm = args.layout == "cm" or (args.layout == "auto" and lo <= args.batch <= hi)
+    if not cm:
+        return "K-major packed [K/2, N] (the reference's format; mma.sync decode GEMV)"
+    return ("tiled column-major, repacked once from the reference's K-major format (tcgen05 decode GEMV) for "
+            "projections with K >= 2048; narrower ones K-major")
+
+
 def _config(args) -> dict:
     tp = args.model != "0.5b"
     par = (f"tp{args.gpus}" if tp else f"replicas{args.gpus}") if args.gpus > 1 else "single"
@@ -279,8 +290,9 @@ def _config(args) -> dict:
     return {"workload": f"Qwen2.5-{args.model.upper()}-shaped int4 g128 greedy decode", "model": f"qwen2.5-{args.model}",
             "batch_per_gpu": args.batch, "prompt_len": args.prompt,
             "global_batch": args.batch if tp else args.batch * args.gpus, "parallelism": par,
-            "weights": ("int4 group-128 K-major, bf16 scales/zeros/activations; embedding, norms and lm_head bf16"
-                        if tp else "int4 group-128 K-major (fp16 scales/zeros); embeddings/norms/lm_head fp16"),
+            "weights": ("int4 group-128, bf16 scales/zeros/activations; embedding, norms and lm_head bf16"
+                        if tp else "int4 group-128 (fp16 scales/zeros); embeddings/norms/lm_head fp16"),
+            "layout": _layout_desc(args),
             "l2": "per-step working set (int4 weights + lm_head) exceeds the 126 MB L2"}
 
 
