@@ -21,10 +21,12 @@ from tritonforge_b200.decode import QwenDecoder, QwenWeights
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name,tp,layers", [("7b", 2, 2), ("72b", 4, 1), ("72b", 2, 1), ("72b", 8, 1)])
-def test_tp_threads_match_tp1(name, tp, layers):
+@pytest.mark.parametrize("name,tp,layers,B", [("7b", 2, 2, 3), ("72b", 4, 1, 3), ("72b", 2, 1, 3), ("72b", 8, 1, 3),
+                                               ("72b", 8, 1, 16), ("7b", 2, 2, 16)])
+def test_tp_threads_match_tp1(name, tp, layers, B):
+    """B = 16 runs the column-major tcgen05 decode kernel on every wide projection."""
     dev = torch.device("cuda", 0)
-    B, T, steps = 3, 64, 3
+    T, steps = 64, 3
     full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=11, layers=layers)
     ref = QwenDecoder(full, B, T)
     ref.fill_cache(20, seed=2)
@@ -78,15 +80,15 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fused", ["1", "0"])
-def test_tp_nccl_matches_tp1(fused):
+@pytest.mark.parametrize("fused,batch", [("1", "4"), ("0", "4"), ("1", "16")])
+def test_tp_nccl_matches_tp1(fused, batch):
     n = 2 if torch.cuda.device_count() < 4 else 4
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(root, "tests", "tp_check.py")]
     env = dict(os.environ, TP_CHECK_MODEL="72b" if n == 4 else "7b", TP_CHECK_LAYERS="1", TP_CHECK_FUSED=fused,
-               NCCL_NVLS_ENABLE="0")
+               TP_CHECK_BATCH=batch, NCCL_NVLS_ENABLE="0")
     p = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
     lines = [l for l in p.stdout.splitlines() if l.startswith("TP_CHECK ")]
     assert p.returncode == 0 and lines, p.stdout[-3000:] + p.stderr[-3000:]
