@@ -157,3 +157,32 @@ def test_allreduce_rmsnorm_validates_without_a_gpu():
                                              8192, 1e-6, _lib.BF16, None, None) == _lib.ERR_BAD_SHAPE
     assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 0, 2, None, None, None, _lib.BF16, None, None, 0,
                                              8192, 1e-6, _lib.BF16, None, None) == _lib.OK
+
+
+def test_colmajor_entry_points_validate_without_a_gpu():
+    """The column-major decode entry points check their arguments before any
+    CUDA call; the layout size is ceil(N/256)*256 x K_pad/2 bytes."""
+    lib = _lib.load()
+    assert lib.tf_int4_cm_bytes(4864, 896) == 19 * 256 * 448
+    assert lib.tf_int4_cm_bytes(256, 128) == 256 * 64
+    assert lib.tf_int4_cm_bytes(0, 128) == 0
+    assert lib.tf_repack_int4_cm(None, None, 64, 200, None) == _lib.ERR_BAD_SHAPE  # K_pad % 128
+    assert b"multiple of 128" in lib.tf_last_error_message()
+    assert lib.tf_repack_int4_cm(None, None, -1, 128, None) == _lib.ERR_BAD_SHAPE
+    assert lib.tf_repack_int4_cm(None, None, 64, 128, None) == _lib.ERR_BAD_ARG  # null pointers
+    assert lib.tf_repack_int4_cm(None, None, 0, 128, None) == 0  # empty: no-op
+    assert lib.tf_qlinear_cm_workspace_bytes(32, 8192, 8192) >= 256
+    # M = 65 is outside the kernel's range: rejected as unsupported before launching
+    x = ctypes.c_void_p(16)
+    rc = lib.tf_qlinear_cm(x, 256, 1, x, x, x, 1, None, 0, x, 128, 65, 128, 256, 256, 128, x, 256, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"M <= 64" in lib.tf_last_error_message()
+    rc = lib.tf_qlinear_cm_swiglu(x, 256, 1, x, x, x, 1, x, 64, 4, 192, 256, 256, 128, x, 256, None)
+    assert rc == _lib.ERR_BAD_SHAPE  # N % 128
+
+
+def test_colmajor_python_layer_checks():
+    from tritonforge_b200 import colmajor
+
+    assert colmajor.cm_shape(4864, 896) == (19, 7, 256, 64)
+    with pytest.raises(RuntimeError):  # no CPU path
+        colmajor.repack_cm(torch.zeros(64, 256, dtype=torch.uint8))
