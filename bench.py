@@ -368,8 +368,14 @@ def run_ours(args) -> None:
         from tritonforge_b200.decode import QwenWeights
 
         args.want_cpu = False
-        weights = QwenWeights.synthetic(args.model, tp=world, rank=rank, dtype=torch.bfloat16, device=dev,
-                                        seed=0)
+        cache_dir = os.path.join(args.weights_cache, f"{args.model}-tp{world}-rank{rank}") if args.weights_cache else None
+        if cache_dir and os.path.exists(os.path.join(cache_dir, "manifest.json")):
+            weights = QwenWeights.load(cache_dir, device=dev)
+        else:
+            weights = QwenWeights.synthetic(args.model, tp=world, rank=rank, dtype=torch.bfloat16, device=dev,
+                                            seed=0)
+            if cache_dir:
+                weights.save(cache_dir)
         lo, hi = QwenDecoder.COLMAJOR_BATCH
         if args.layout == "cm" or (args.layout == "auto" and lo <= args.batch <= hi):
             weights.to_colmajor()  # in place: one copy of the weights in HBM
@@ -505,6 +511,9 @@ def main() -> None:
                     help="tensor parallel: fused all-reduce + RMSNorm over peer memory, or NCCL + RMSNorm")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights-cache", default=None,
+                    help="directory of saved int4 shards (one subdirectory per model, TP degree and rank): "
+                         "loaded when present, else generated and saved there")
     ap.add_argument("--layout", choices=["auto", "cm", "kmajor"], default="auto",
                     help="int4 weight layout of the decode projections: tiled column-major (tcgen05 kernel), "
                          "the reference's K-major (mma.sync kernel), or auto (column-major for batches 9..64)")

@@ -216,6 +216,19 @@ class QwenWeights:
             out.append(d)
         return out
 
+    def save(self, path: str) -> None:
+        """Write these (K-major) weights to a directory: see shard_cache."""
+        from .shard_cache import save_weights
+
+        save_weights(self, path)
+
+    @classmethod
+    def load(cls, path: str, device=None) -> "QwenWeights":
+        """Weights written by `save`, on `device` (default: current CUDA device)."""
+        from .shard_cache import load_weights
+
+        return load_weights(path, device)
+
     def to_colmajor(self, min_k: int = 2048) -> "QwenWeights":
         """`colmajor_layers` in place: the K-major packed tensors are dropped
         (memory for one copy of the weights). Shard before converting."""
