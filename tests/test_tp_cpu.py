@@ -197,3 +197,17 @@ def test_vocab_parallel_argmax_gloo(world):
         p.join(timeout=60)
     for rank, ok, info in results:
         assert ok, (rank, info)
+
+
+def test_token_flip_gap_bound():
+    """The TP token check accepts a flip only inside twice the logit tolerance."""
+    import torch
+
+    from tests.tp_check import token_flip_gap
+
+    ref = torch.tensor([[1.00, 0.99, 0.0], [2.0, 1.0, 0.5]])
+    ref_tok = torch.tensor([0, 0])
+    gap, bound = token_flip_gap(ref, ref_tok, torch.tensor([1, 0]), rms=1.0)
+    assert abs(gap - 0.01) < 1e-6 and gap <= bound
+    gap, bound = token_flip_gap(ref, ref_tok, torch.tensor([0, 1]), rms=1.0)
+    assert abs(gap - 1.0) < 1e-6 and gap > bound
