@@ -67,8 +67,11 @@ const char* tf_last_error_message(void);
  * bias (any of fp16/bf16/fp32, or NULL) is added and rounded again -- the
  * rounding points of the reference oracle (reference.py:21-36).
  * `workspace` must hold tf_qlinear_workspace_bytes(...) bytes and be zeroed
- * once before its first use; calls leave it zeroed. Calls that share a
- * workspace must be ordered on one stream.
+ * once before its first use. Word 0 is the error word of the kernels' bounded
+ * waits: a wait that gives up (1 s) sets a bit there and the call still
+ * returns TF_OK, so read it with tf_workspace_error; it stays set until the
+ * caller clears it. Calls that share a workspace must be ordered on one
+ * stream.
  */
 size_t tf_qlinear_workspace_bytes(int64_t M, int64_t N, int64_t K_pad, int32_t group_size);
 
@@ -96,13 +99,24 @@ int tf_qlinear_ex(const void* x, int64_t ldx, int x_dtype,
  * TF_ERR_WORKSPACE. The first call on each device sets the array up (looks up
  * its device address, clears it on `stream`), so make it before any stream
  * capture. All calls share the array: calls that can overlap on the GPU race,
- * order them on one stream. Allocates nothing. */
+ * order them on one stream. Allocates nothing. A bounded device wait that
+ * gives up does not change the return code: read it with
+ * tf_qlinear_noalloc_error. */
 int tf_qlinear_noalloc(const void* x, int64_t ldx, int x_dtype,
                        const uint8_t* packed, const void* scales, const void* zeros, int param_dtype,
                        const void* bias, int bias_dtype,
                        void* out, int64_t ldo,
                        int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
                        void* stream);
+
+/* The error word of tf_qlinear_noalloc's built-in scratch on the current
+ * device (no counterpart in the reference): a bounded device-side wait of any
+ * tf_qlinear_noalloc call that gave up set a bit there, while that call still
+ * returned TF_OK. Copies the word to *error_out (blocking on `stream`), clears
+ * it on the device when `clear` is non-zero and the word was set, and returns
+ * TF_ERR_TIMEOUT when it was set, TF_OK otherwise. Order it after the calls it
+ * should cover (same stream). Allocates nothing. */
+int tf_qlinear_noalloc_error(int* error_out, int clear, void* stream);
 
 /* Reads the device-side error word of a workspace (blocking copy on `stream`):
  * 0 when every kernel that used it completed its bounded waits. */
@@ -239,6 +253,25 @@ int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t*
                          const void* zeros, int param_dtype, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
                          int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tf_qlinear_partial / tf_qlinear_cm_partial: the int4 linear of a
+ * row-parallel tensor-parallel projection (o_proj, down_proj sharded on K):
+ * out[M, N] (fp32, row stride ldo) = x @ W with the fp32 sums stored
+ * unrounded and no bias. Each rank's partial is then added across ranks in
+ * fp32 and rounded once (tf_allreduce_rmsnorm_residual with TF_F32 partials),
+ * so a tensor-parallel layer rounds where the single-GPU layer rounds (no
+ * reference counterpart: the reference is single-GPU; replaces the sharded
+ * half of quantized_linear, reference src/tritonforge/kernels/
+ * dequant_gemm.py:151-210). tf_qlinear_partial takes the reference's packed
+ * layout (any regime), tf_qlinear_cm_partial the tiled column-major layout
+ * (constraints of tf_qlinear_cm). Workspace as tf_qlinear. */
+int tf_qlinear_partial(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
+                       const void* zeros, int param_dtype, float* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                       int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+int tf_qlinear_cm_partial(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm, const void* scales,
+                          const void* zeros, int param_dtype, float* out, int64_t ldo, int64_t M, int64_t N,
+                          int64_t K, int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* tf_allreduce_rmsnorm_residual: tensor-parallel all-reduce of row-parallel
  * partial sums fused with residual-add + RMSNorm (no reference counterpart:
  * the reference is single-GPU; it replaces an all-reduce followed by
@@ -249,6 +282,8 @@ int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t*
  *   offset_bytes         this call's partial tile [M, N] inside every buffer
  *   pad_slot             first signal-pad slot used (pad_slot .. pad_slot + world - 1)
  *   counters             this rank's device u32[2], zeroed once before the first call
+ *   partial_dtype        TF_F32 (the unrounded sums of tf_qlinear_partial;
+ *                        offset_bytes % 32 == 0) or `dtype`
  * Computes o = round(sum_r partial_r) (fp32 sum in rank order, identical on
  * every rank), summed = round(o + residual), normed = round(round(summed *
  * rstd) * weight). Waits for the peers' signals at most 1 s; on expiry sets
@@ -258,7 +293,7 @@ int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const uint64_t* 
                                   int64_t offset_bytes, int32_t pad_slot, int32_t rank, int32_t world,
                                   uint32_t* counters, const void* residual, const void* weight, int w_dtype,
                                   void* normed, void* summed, int64_t M, int64_t N, float eps, int dtype,
-                                  int* error_word, void* stream);
+                                  int partial_dtype, int* error_word, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -89,6 +89,45 @@ def _rotate(t: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tens
     return t * cos + rot * sin
 
 
+def random_int4_linear(n: int, k: int, gen: torch.Generator, dtype: torch.dtype, bias: bool = False,
+                       group_size: int = 128):
+    """An int4 linear [k -> n] in the reference's format with seeded random
+    contents: codes uniform in 0..15 packed K-major (quant.py:25-63 layout),
+    scales |N(0, 0.02)| x 4 / 15 (the range of N(0, 0.02) weights over 15
+    steps), zeros uniform in 0..15, all on the host. For CPU timing samples,
+    whose cost does not depend on the values; built without any GPU code."""
+    k_pad = -(-k // group_size) * group_size
+    packed = torch.randint(0, 256, (k_pad // 2, n), generator=gen, dtype=torch.uint8).numpy()
+    scales = (torch.randn(k_pad // group_size, n, generator=gen).abs() * 0.02 * 4 / 15 + 1e-4).to(dtype)
+    zeros = torch.randint(0, 16, (k_pad // group_size, n), generator=gen).to(dtype)
+    b = (torch.randn(n, generator=gen) * 0.02).to(dtype) if bias else None
+    return OracleQuantLinear(packed, scales, zeros, k, n, b, group_size)
+
+
+def quantize_model_on_cpu(model: nn.Module, group_size: int = 128, dtype: torch.dtype = torch.float16) -> nn.Module:
+    """The reference's patched model on the host: every q/k/v/o/gate/up/down
+    Linear of a transformers Qwen2 model quantised by the oracle quantizer
+    (bit-exact with quant.py:29-63) into an OracleQuantLinear, the MLP
+    activation the SwiGLU oracle (integration/qwen.py:57-80 with
+    fuse_max_m=0). Modifies and returns `model` (kept on the CPU)."""
+    model = model.to("cpu")
+    npdt = _NP[dtype]
+    for layer in model.model.layers:
+        for parent, names in ((layer.self_attn, ("q_proj", "k_proj", "v_proj", "o_proj")),
+                              (layer.mlp, ("gate_proj", "up_proj", "down_proj"))):
+            for name in names:
+                lin = getattr(parent, name)
+                packed, s_bits, z_bits, _ = oquant.quantize_int4_group(lin.weight.detach().float().numpy(),
+                                                                       group_size, npdt)
+                scales = torch.from_numpy(oquant.half_bits_to_f32(s_bits, npdt)).to(dtype)
+                zeros = torch.from_numpy(oquant.half_bits_to_f32(z_bits, npdt)).to(dtype)
+                bias = None if lin.bias is None else lin.bias.detach().to(dtype)
+                setattr(parent, name, OracleQuantLinear(packed, scales, zeros, lin.in_features, lin.out_features,
+                                                        bias, group_size))
+        layer.mlp.forward = types.MethodType(_swiglu_mlp_forward, layer.mlp)
+    return model.eval()
+
+
 class CpuLayer:
     """One Qwen2 decoder layer of int4 weights on the CPU, computed the
     reference's way: dequantize-then-matmul projections (qwen.py:91-97),
@@ -97,6 +136,8 @@ class CpuLayer:
 
     def __init__(self, layer: dict, hidden: int, q_heads: int, kv_heads: int, head_dim: int, eps: float):
         def ql(q) -> OracleQuantLinear:
+            if isinstance(q, OracleQuantLinear):
+                return q
             return OracleQuantLinear(q.packed.cpu().numpy(), q.scales.cpu(), q.zeros.cpu(), q.in_features,
                                      q.out_features, None if q.bias is None else q.bias.cpu(), q.group_size)
 
@@ -130,3 +171,18 @@ class CpuLayer:
         gate, up = gu[:, :self.inter], gu[:, self.inter:]
         act = ((gate * torch.sigmoid(gate)) * up).to(x.dtype)
         return x + self.down(act)
+
+    @classmethod
+    def random(cls, hidden: int, inter: int, q_heads: int, kv_heads: int, head_dim: int, eps: float,
+               dtype: torch.dtype = torch.bfloat16, seed: int = 0) -> "CpuLayer":
+        """A layer of the given shape with seeded random int4 contents
+        (random_int4_linear: q|k|v with bias, gate|up concatenated), built on
+        the host without any GPU code: the timing sample of a model too large
+        for the CPU."""
+        g = torch.Generator().manual_seed(seed)
+        qkv = random_int4_linear((q_heads + 2 * kv_heads) * head_dim, hidden, g, dtype, bias=True)
+        layer = {"qkv": qkv, "o": random_int4_linear(hidden, q_heads * head_dim, g, dtype),
+                 "gu": random_int4_linear(2 * inter, hidden, g, dtype),
+                 "down": random_int4_linear(hidden, inter, g, dtype),
+                 "in_norm": torch.ones(hidden, dtype=dtype), "post_norm": torch.ones(hidden, dtype=dtype)}
+        return cls(layer, hidden, q_heads, kv_heads, head_dim, eps)

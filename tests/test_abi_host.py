@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.tf_abi_version() == 1
+    assert lib.tf_abi_version() == 2
     assert lib.tf_status_string(0) == b"ok"
     assert lib.tf_status_string(_lib.ERR_WORKSPACE).startswith(b"workspace")
     assert lib.tf_status_string(99) == b"unknown status"
@@ -152,11 +152,11 @@ def test_allreduce_rmsnorm_validates_without_a_gpu():
     lib = _lib.load()
     # null pointers / rank outside the group are rejected before anything is launched
     assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 0, 2, None, None, None, _lib.BF16, None, None, 4,
-                                             8192, 1e-6, _lib.BF16, None, None) == _lib.ERR_BAD_ARG
+                                             8192, 1e-6, _lib.BF16, _lib.F32, None, None) == _lib.ERR_BAD_ARG
     assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 3, 2, None, None, None, _lib.BF16, None, None, 4,
-                                             8192, 1e-6, _lib.BF16, None, None) == _lib.ERR_BAD_SHAPE
+                                             8192, 1e-6, _lib.BF16, _lib.F32, None, None) == _lib.ERR_BAD_SHAPE
     assert lib.tf_allreduce_rmsnorm_residual(None, None, 0, 64, 0, 2, None, None, None, _lib.BF16, None, None, 0,
-                                             8192, 1e-6, _lib.BF16, None, None) == _lib.OK
+                                             8192, 1e-6, _lib.BF16, _lib.F32, None, None) == _lib.OK
 
 
 def test_colmajor_entry_points_validate_without_a_gpu():

@@ -24,9 +24,9 @@ pytestmark = pytest.mark.gpu
 SLOT = 64
 
 
-def _make(world, m, n, dtype, seed):
+def _make(world, m, n, dtype, seed, part_dtype=None):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    parts = [(torch.randn(m, n, device="cuda", generator=g) * 0.5).to(dtype) for _ in range(world)]
+    parts = [(torch.randn(m, n, device="cuda", generator=g) * 0.5).to(part_dtype or dtype) for _ in range(world)]
     pads = [torch.zeros(SLOT + 8, dtype=torch.int32, device="cuda") for _ in range(world)]
     res = torch.randn(m, n, device="cuda", generator=g).to(dtype)
     w = (1 + 0.02 * torch.randn(n, device="cuda", generator=g)).to(dtype)
@@ -35,19 +35,23 @@ def _make(world, m, n, dtype, seed):
     return parts, pads, res, w, bufs, pad_ptrs
 
 
-def _call(bufs, pad_ptrs, world, ctr, res, w, normed, summed, err, dtype):
+def _call(bufs, pad_ptrs, world, ctr, res, w, normed, summed, err, dtype, part_dtype=None):
     m, n = res.shape
     rc = _lib.load().tf_allreduce_rmsnorm_residual(
         bufs.data_ptr(), pad_ptrs.data_ptr(), 0, SLOT, 0, world, ctr.data_ptr(), res.data_ptr(), w.data_ptr(),
         _lib.dtype_code(w.dtype), normed.data_ptr(), summed.data_ptr(), m, n, 1e-6, _lib.dtype_code(dtype),
-        err.data_ptr(), _lib.stream_ptr(res.device))
+        _lib.dtype_code(part_dtype or dtype), err.data_ptr(), _lib.stream_ptr(res.device))
     _lib.check(rc, "allreduce_rmsnorm_residual")
 
 
+@pytest.mark.parametrize("partials", ["fp32", "model"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("world,m,n", [(1, 4, 896), (2, 32, 8192), (4, 8, 3584), (8, 3, 8192)])
-def test_fused_allreduce_rmsnorm(world, m, n, dtype):
-    parts, pads, res, w, bufs, pad_ptrs = _make(world, m, n, dtype, seed=world * 10 + m)
+def test_fused_allreduce_rmsnorm(world, m, n, dtype, partials):
+    """fp32 partials (tf_qlinear_partial's unrounded sums, what the decoder
+    hands over) and partials already rounded to the model dtype."""
+    pdt = torch.float32 if partials == "fp32" else dtype
+    parts, pads, res, w, bufs, pad_ptrs = _make(world, m, n, dtype, seed=world * 10 + m, part_dtype=pdt)
     ctr = torch.zeros(2, dtype=torch.int32, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     normed = torch.empty_like(res)
@@ -56,7 +60,7 @@ def test_fused_allreduce_rmsnorm(world, m, n, dtype):
     for call in (1, 2, 3):
         for p in range(1, world):
             pads[0][SLOT + p] = call  # peer p has signalled this call
-        _call(bufs, pad_ptrs, world, ctr, res, w, normed, summed, err, dtype)
+        _call(bufs, pad_ptrs, world, ctr, res, w, normed, summed, err, dtype, pdt)
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         assert int(ctr[0].item()) == call and int(ctr[1].item()) == 0

@@ -10,8 +10,8 @@ import pytest
 import torch
 
 from oracle import quant as oquant
-from tests.parity import assert_rms_close, assert_swiglu_close, oracle_linear
-from tritonforge_b200 import _lib, colmajor, quant
+from tests.parity import assert_rms_close, assert_swiglu_close, f32, oracle_linear
+from tritonforge_b200 import _lib, colmajor, kernels, quant
 from tritonforge_b200.tp import interleave_gate_up
 
 pytestmark = pytest.mark.gpu
@@ -130,3 +130,53 @@ def test_decoder_colmajor_matches_kmajor(batch):
     eager = b.step().clone()
     b.tokens.copy_(saved[0]); b.pos.copy_(saved[1]); b.k_cache.copy_(saved[2]); b.v_cache.copy_(saved[3])
     assert torch.equal(b.replay().clone(), eager)
+
+
+@pytest.mark.parametrize("layout,regime,m", [("kmajor", "gemv", 1), ("kmajor", "gemv", 16), ("kmajor", "gemv", 32),
+                                              ("kmajor", "gemm", 64), ("kmajor", "simt", 5), ("cm", "cm", 1),
+                                              ("cm", "cm", 32), ("cm", "cm", 64)])
+def test_qlinear_partial_is_the_unrounded_sum(layout, regime, m):
+    """tf_qlinear_partial / tf_qlinear_cm_partial (a row-parallel shard's fp32
+    partial): the fp32 sums of the same kernel, not rounded, no bias. Rounded
+    once they equal the regular entry point's output bit for bit; against a
+    float64 sum of the oracle's dequantised weights they are fp32-accurate."""
+    dtype = torch.bfloat16
+    k, n = 2048, 1024
+    g = torch.Generator().manual_seed(m + 7)
+    x = torch.randn(m, k, generator=g).to(dtype).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).cuda()
+    packed, scales, zeros, _ = quant.quantize_int4_group(w, 128, dtype)
+    lib = _lib.load()
+    ws = _lib.workspaces.get(x.device, 256)
+    part = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    if layout == "cm":
+        tiles = colmajor.repack_cm(packed)
+        want = colmajor.quantized_linear_cm(x, tiles, scales, zeros)
+        rc = lib.tf_qlinear_cm_partial(x.data_ptr(), k, _lib.BF16, tiles.data_ptr(), scales.data_ptr(),
+                                       zeros.data_ptr(), _lib.BF16, part.data_ptr(), n, m, n, k, k, 128,
+                                       ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device))
+    else:
+        want = kernels.quantized_linear(x, packed, scales, zeros, None, 128, {"regime": regime})
+        if regime == "gemv":
+            rc = lib.tf_qlinear_partial(x.data_ptr(), k, _lib.BF16, packed.data_ptr(), scales.data_ptr(),
+                                        zeros.data_ptr(), _lib.BF16, part.data_ptr(), n, m, n, k, k, 128,
+                                        ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device))
+        else:
+            # the partial entry point picks its regime like tf_qlinear; force the others by shape:
+            # simt through an odd stride (ldx not a multiple of 8), gemm through M > 32
+            xs = x
+            if regime == "simt":
+                xs = torch.zeros(m, k + 1, dtype=dtype, device="cuda")[:, :k]
+                xs.copy_(x)
+            rc = lib.tf_qlinear_partial(xs.data_ptr(), xs.stride(0), _lib.BF16, packed.data_ptr(),
+                                        scales.data_ptr(), zeros.data_ptr(), _lib.BF16, part.data_ptr(), n, m, n, k,
+                                        k, 128, ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device))
+    _lib.check(rc, "qlinear_partial")
+    torch.cuda.synchronize()
+    assert torch.isfinite(part).all()
+    assert torch.equal(part.to(dtype), want), "rounded partial differs from the regular entry point"
+    deq = oquant.round_to(oquant.dequantize_int4_f32(packed.cpu().numpy(), f32(scales), f32(zeros), 128), "bfloat16")
+    exact = f32(x).astype(np.float64) @ np.asarray(deq, np.float64)[:k]
+    err = np.abs(f32(part).astype(np.float64) - exact).max()
+    assert err <= 1e-5 * np.abs(exact).max(), err
+    assert _lib.workspaces.errors(x.device) == 0

@@ -72,8 +72,24 @@ def test_rejects_foreign_and_truncated(tmp_path):
     with pytest.raises(ValueError, match="not a"):
         QwenWeights.load(str(tmp_path), device="cpu")
     json.dump(man, open(tmp_path / "manifest.json", "w"))
+    # a shard of another tensor-parallel degree or rank is refused
+    with pytest.raises(ValueError, match="wanted tp=2"):
+        QwenWeights.load(str(tmp_path), device="cpu", tp=2, rank=0)
+    with pytest.raises(ValueError, match="rank=1"):
+        QwenWeights.load(str(tmp_path), device="cpu", tp=1, rank=1)
+    QwenWeights.load(str(tmp_path), device="cpu", tp=1, rank=0)
+    # another layout of the fused projections is refused
+    json.dump(dict(man, layout={"gu": "gate then up"}), open(tmp_path / "manifest.json", "w"))
+    with pytest.raises(ValueError, match="another layout"):
+        QwenWeights.load(str(tmp_path), device="cpu")
+    json.dump(man, open(tmp_path / "manifest.json", "w"))
+    # a blob that does not belong to its manifest (an interrupted save) is refused
     size = os.path.getsize(tmp_path / "tensors.bin")
     with open(tmp_path / "tensors.bin", "r+b") as f:
         f.truncate(size - 100)
+    with pytest.raises(ValueError, match="does not match its manifest"):
+        QwenWeights.load(str(tmp_path), device="cpu")
+    # a manifest that claims the short blob still stops at the tensor that runs past the end
+    json.dump(dict(man, blob_bytes=size - 100), open(tmp_path / "manifest.json", "w"))
     with pytest.raises(ValueError, match="past the end"):
         QwenWeights.load(str(tmp_path), device="cpu")

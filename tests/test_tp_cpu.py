@@ -199,15 +199,25 @@ def test_vocab_parallel_argmax_gloo(world):
         assert ok, (rank, info)
 
 
-def test_token_flip_gap_bound():
-    """The TP token check accepts a flip only inside twice the logit tolerance."""
+def test_near_tie_check():
+    """The TP token check accepts a differing greedy token only where the
+    reference scores it within the contract's 2e-2 x RMS of its own choice."""
     import torch
 
-    from tests.tp_check import token_flip_gap
+    from tests.tp_check import logits_close, near_tie
 
     ref = torch.tensor([[1.00, 0.99, 0.0], [2.0, 1.0, 0.5]])
     ref_tok = torch.tensor([0, 0])
-    gap, bound = token_flip_gap(ref, ref_tok, torch.tensor([1, 0]), rms=1.0)
-    assert abs(gap - 0.01) < 1e-6 and gap <= bound
-    gap, bound = token_flip_gap(ref, ref_tok, torch.tensor([0, 1]), rms=1.0)
-    assert abs(gap - 1.0) < 1e-6 and gap > bound
+    ok, gap = near_tie(ref, ref_tok, torch.tensor([1, 0]), rms=1.0)
+    assert ok and abs(gap - 0.01) < 1e-6
+    ok, gap = near_tie(ref, ref_tok, torch.tensor([0, 1]), rms=1.0)
+    assert not ok and abs(gap - 1.0) < 1e-6
+    assert near_tie(ref, ref_tok, ref_tok, rms=1.0) == (True, 0.0)
+    # logits: max-abs against 2e-2 x RMS, mean against a tenth of it
+    base = torch.randn(4, 1000, generator=torch.Generator().manual_seed(0))
+    rms = float(base.pow(2).mean().sqrt())
+    bumped = base.clone()
+    bumped[0, 0] += 0.015 * rms
+    assert logits_close(bumped, base)[0]
+    bumped[0, 1] += 0.03 * rms
+    assert not logits_close(bumped, base)[0]

@@ -1,7 +1,8 @@
 """GPU tests of tensor-parallel decode: shards of the same int4 weights,
 decoded as TP ranks (threads on one GPU, or NCCL ranks on several GPUs),
-match a tp=1 decode of the full weights within bf16 rounding noise (see
-tests.tp_check.logits_close), and the ranks agree bit for bit."""
+match a tp=1 decode of the full weights within the bf16 contract (max-abs
+<= 2e-2 x RMS of the logits, tests.tp_check.logits_close), and the ranks
+agree bit for bit."""
 
 from __future__ import annotations
 
@@ -58,9 +59,10 @@ def test_tp_threads_match_tp1(name, tp, layers, B):
         for d in decs[1:]:
             assert torch.equal(d.buf["logits"], decs[0].buf["logits"])
         ok, err, rms = logits_close(decs[0].buf["logits"], ref.buf["logits"])
-        assert ok, f"tp{tp} logits: max-abs beyond 4 ulps {err:.4g} (tolerance 6e-2 x RMS {rms:.4g})"
+        assert ok, f"tp{tp} logits: max-abs {err:.4g} > 2e-2 x RMS {rms:.4g}"
         for d in decs:
             d.tokens.copy_(ref.tokens)
+    assert all(d.device_errors() == 0 for d in decs) and ref.device_errors() == 0
 
 
 def test_shard_tp1_is_identity():

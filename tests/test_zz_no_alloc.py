@@ -4,8 +4,10 @@ device memory, a host runtime behind an FFI with no CUDA allocator): it takes
 its scratch from an array built into the library instead of a workspace.
 
 It is called here through the C ABI and its output is compared with the
-regular entry point's (tf_qlinear through kernels.quantized_linear) on two
-calls in a row, with the parity tolerance of the other tests. This file is
+regular entry point's (tf_qlinear through kernels.quantized_linear) and with
+the oracle, on two calls in a row, with the parity tolerance of the other
+tests; after the calls the array's error word (tf_qlinear_noalloc_error) must
+be 0, i.e. every bounded device wait of those calls completed. This file is
 collected last so that a run stopping at the first failure has run everything
 else first; it also passes when run alone in a fresh process (the first call
 sets the array up).
@@ -13,10 +15,12 @@ sets the array up).
 
 from __future__ import annotations
 
+import ctypes
+
 import pytest
 import torch
 
-from tests.parity import assert_rms_close
+from tests.parity import assert_rms_close, oracle_linear
 from tritonforge_b200 import _lib, kernels, quant
 
 pytestmark = pytest.mark.gpu
@@ -47,8 +51,13 @@ def test_noalloc_matches_regular_entry_point(m, n, k, dtype):
     packed, scales, zeros, _ = quant.quantize_int4_group(w, 128, dtype)
     bias = torch.randn(n, generator=g).to(dtype).cuda()
     want = kernels.quantized_linear(x, packed, scales, zeros, bias)
+    ref = oracle_linear(x, packed, scales, zeros, bias)
     for _ in range(2):  # the shared scratch keeps the previous call's contents
         out = torch.full((m, n), float("nan"), dtype=dtype, device="cuda")
         got = _noalloc(x, packed, scales, zeros, bias, out)
         torch.cuda.synchronize()
-        assert_rms_close(got, want.float().cpu().numpy(), dtype, f"noalloc {m}x{n}x{k}")
+        assert_rms_close(got, want.float().cpu().numpy(), dtype, f"noalloc {m}x{n}x{k} vs tf_qlinear")
+        assert_rms_close(got, ref, dtype, f"noalloc {m}x{n}x{k} vs oracle")
+    word = ctypes.c_int(-1)
+    rc = _lib.load().tf_qlinear_noalloc_error(ctypes.byref(word), 1, _lib.stream_ptr(x.device))
+    assert rc == _lib.OK and word.value == 0, (rc, word.value)

@@ -1,7 +1,8 @@
 """Tensor-parallel decode checks shared by the GPU tests.
 
-`ThreadReducer` emulates TP ranks as threads on one GPU (host barrier, sum on
-device in the model dtype, like a 2-rank NCCL ring); run as a script under
+`ThreadReducer` emulates TP ranks as threads on one GPU (host barrier, the
+fp32 partials summed on the device in rank order, as the fused all-reduce
+does); run as a script under
 torchrun this module is the NCCL worker: every rank builds the same full
 weights, decodes its shard with the all-reduce captured in a CUDA graph, and
 rank 0 compares the logits with a tp=1 decode of the full weights.
@@ -63,43 +64,36 @@ def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
     dst.pos.copy_(src.pos)
 
 
-def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 6e-2, ulps: int = 4) -> tuple[bool, float, float]:
-    """Tensor-parallel logits against tp=1 logits of the same weights.
+def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> tuple[bool, float, float]:
+    """Tensor-parallel logits against tp=1 logits of the same weights, with
+    the bf16 contract: max |got - ref| <= tol x RMS(ref), and the mean
+    difference at most a tenth of that.
 
-    Row-parallel partial sums are rounded to bf16 before the all-reduce adds
-    them (one extra rounding of the residual stream per row-parallel layer),
-    so logits may differ by a few bf16 ulps of their own magnitude: a logit
-    near 10 has an ulp of 0.0625, 5% of an RMS near 1.2. A relative hidden-state
-    difference of 2^-8 moves a logit by about 2^-8 x RMS; over 10^5-10^6
-    logits the largest such move is ~5 sigma, 2% of the RMS. The check is
-    max(|got - ref| - ulps x ulp(ref)) <= tol x RMS(ref) and mean
-    |got - ref| <= tol / 6 x RMS(ref) (typical differences stay at rounding
-    level)."""
+    Row-parallel projections hand the all-reduce unrounded fp32 partials,
+    which are added in fp32 and rounded once, as the single-GPU projection
+    rounds its full sum; what remains is the fp32 summation order (sharded
+    split-K sums, then the cross-rank sum), which moves a rounded bf16 value by
+    one ulp now and then."""
     ref32 = ref.float()
-    ulp = torch.ldexp(torch.ones_like(ref32), torch.frexp(ref32)[1] - 8)  # bf16 ulp of each value
     diff = (got.float() - ref32).abs()
-    err = float((diff - ulps * ulp).clamp_min(0).max())
+    err = float(diff.max())
     rms = float(ref32.pow(2).mean().sqrt())
     mean = float(diff.mean())
-    return err <= tol * rms and mean <= tol / 6 * rms, err, rms
+    return err <= tol * rms and mean <= tol / 10 * rms, err, rms
 
 
-def token_flip_gap(ref_logits: torch.Tensor, ref_tok: torch.Tensor, got_tok: torch.Tensor, rms: float,
-                   tol: float = 6e-2, ulps: int = 4) -> tuple[float, float]:
-    """A greedy token that differs from the reference's is explained by the
-    logit tolerance when the reference scores the chosen token within two
-    logit errors of its own choice: if every logit is within tol x RMS (+ ulps)
-    of the reference (the logits_close bound), the two logits involved can
-    close a reference gap of at most twice that. Returns (largest reference
-    gap over the rows that differ, that bound)."""
-    import math
-
+def near_tie(ref_logits: torch.Tensor, ref_tok: torch.Tensor, got_tok: torch.Tensor, rms: float,
+             tol: float = 2e-2) -> tuple[bool, float]:
+    """Rows whose greedy tokens differ must be genuine near-ties of the
+    reference: the reference scores the other token within tol x RMS of its
+    own choice. Returns (whether all differing rows are such ties, the largest
+    reference gap among them)."""
     ref32 = ref_logits.float()
     rows = (got_tok != ref_tok).nonzero().flatten()
-    top = ref32[rows, ref_tok[rows]]
-    gap = float((top - ref32[rows, got_tok[rows]]).max())
-    ulp = 2.0 ** (math.frexp(float(top.abs().max()))[1] - 8)  # bf16 ulp of the largest logit involved
-    return gap, 2 * (tol * rms + ulps * ulp)
+    if rows.numel() == 0:
+        return True, 0.0
+    gap = float((ref32[rows, ref_tok[rows]] - ref32[rows, got_tok[rows]]).max())
+    return gap <= tol * rms, gap
 
 
 def _nccl_main() -> int:
@@ -131,11 +125,9 @@ def _nccl_main() -> int:
         dec.graph.replay()
         ok, err, rms = logits_close(dec.buf["logits"], ref.buf["logits"][:, v0:v0 + nv])
         same_tok = bool(torch.equal(dec.tokens, ref.tokens))
-        gap = 0.0
-        if not same_tok:
-            gap, bound = token_flip_gap(ref.buf["logits"], ref.tokens, dec.tokens, rms)
-            ok &= gap <= bound
-        report["steps"].append({"err": err, "rms": rms, "tokens_equal": same_tok, "flip_gap": gap})
+        tie_ok, gap = near_tie(ref.buf["logits"], ref.tokens, dec.tokens, rms)
+        ok &= tie_ok
+        report["steps"].append({"err": err, "rms": rms, "tokens_equal": same_tok, "tie_gap": gap})
         report["ok"] &= ok
         # ranks must agree on the tokens bit for bit
         gathered = [torch.empty_like(dec.tokens) for _ in range(world)]
@@ -144,8 +136,8 @@ def _nccl_main() -> int:
         dec.tokens.copy_(ref.tokens)  # keep the two decodes on the same tokens
     report["ranks_identical"] = same_all
     report["fused_allreduce"] = dec.fused_allreduce
-    report["allreduce_errors"] = dec.allreduce_errors()
-    report["ok"] &= report["allreduce_errors"] == 0
+    report["device_errors"] = dec.device_errors() | ref.device_errors()
+    report["ok"] &= report["device_errors"] == 0
     report["ok"] &= report["ranks_identical"]
     torch.cuda.synchronize()
     dec.release()

@@ -44,6 +44,7 @@ SIGNATURES = {
                              _i64, _i64, _i64, _i64, _i32, _vp, _sz, _i32, _vp]),
     "tf_qlinear_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
                                   _i64, _i64, _i64, _i64, _i32, _vp]),
+    "tf_qlinear_noalloc_error": (_i32, [ctypes.POINTER(ctypes.c_int), _i32, _vp]),
     "tf_workspace_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "tf_rmsnorm_residual": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _f32, _i32, _vp]),
     "tf_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp]),
@@ -66,7 +67,11 @@ SIGNATURES = {
     "tf_qlinear_cm_swiglu": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                     _vp, _sz, _vp]),
     "tf_allreduce_rmsnorm_residual": (_i32, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp,
-                                             _i64, _i64, _f32, _i32, _vp, _vp]),
+                                             _i64, _i64, _f32, _i32, _i32, _vp, _vp]),
+    "tf_qlinear_partial": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
+                                  _vp, _sz, _vp]),
+    "tf_qlinear_cm_partial": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
+                                     _vp, _sz, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -138,10 +143,10 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 class _Workspaces:
     """Zero-initialised scratch handed to the kernels, one buffer per (device,
-    stream): its header holds the device error word of the bounded waits, and
-    the column-major decode kernel keeps the arrival counters and partial
-    tiles of split column blocks after it (left zeroed by every call). Calls
-    that share a buffer are therefore ordered on their stream.
+    stream). The kernels use only its 256-byte header: word 0 is the device
+    error word of their bounded waits (a wait that gives up after 1 s sets a
+    bit there and the launch still reports success). Calls that share a buffer
+    are ordered on their stream. ``errors`` reads the word of every buffer.
 
     A buffer is zeroed only when it is (re)allocated. Reallocation happens
     outside any CUDA-graph capture: callers that capture size it first with
@@ -163,6 +168,21 @@ class _Workspaces:
 
     def reserve(self, device: torch.device, nbytes: int) -> None:
         self.get(device, nbytes)
+
+    def errors(self, device: torch.device | None = None, clear: bool = False) -> int:
+        """OR of the error words of this process's workspaces (on `device`, or
+        all devices): 0 when every kernel that used them completed its bounded
+        waits. Synchronises the devices involved; `clear` zeroes the words."""
+        bits = 0
+        for (idx, _), buf in list(self._bufs.items()):
+            if device is not None and device.index is not None and idx != device.index:
+                continue
+            torch.cuda.synchronize(idx)
+            word = buf[:4].view(torch.int32)
+            bits |= int(word.item())
+            if clear:
+                word.zero_()
+        return bits
 
 
 workspaces = _Workspaces()

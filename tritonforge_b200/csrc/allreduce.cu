@@ -6,6 +6,9 @@
 // all-reduce it and then run `rmsnorm_residual` (integration/qwen.py:145-150
 // and the next layer's input norm). Here one kernel does both:
 //   o      = round(sum over ranks of the partials)      fp32 sum, rank order
+// (the partials are the unrounded fp32 sums of tf_qlinear_partial, so o is
+// rounded once, where a single GPU rounds its full sum; 16-bit partials of the
+// activation type are accepted as well)
 //   summed = round(o + residual)                         (the new residual)
 //   normed = round(round(summed * rstd) * weight)        rstd of the rounded sum
 // with the rounding points of reference.py:39-50. Every rank sums the same
@@ -70,10 +73,23 @@ struct ArArgs {
   float eps;
 };
 
+// 8 consecutive partial values of one peer as fp32: 16 bytes of a 16-bit
+// partial, 32 bytes of an fp32 partial
+template <typename P>
+struct Part8 {
+  uint4 raw[sizeof(P) / 2];
+  __device__ __forceinline__ void load(const uint8_t* p) {
+#pragma unroll
+    for (int i = 0; i < (int)(sizeof(P) / 2); ++i) raw[i] = ld_peer(p + 16 * i);
+  }
+  __device__ __forceinline__ float get(int i) const { return Num<P>::to_f(reinterpret_cast<const P*>(raw)[i]); }
+};
+
 // One cluster of `gridDim.y` CTAs per row: CTA c reduces and normalises
 // columns [c * 8 * VPT * kThreads, ...) of the row, the row's sum of squares is
-// combined through distributed shared memory in CTA-rank order.
-template <typename T, typename TW, int VPT>
+// combined through distributed shared memory in CTA-rank order. P is the type
+// of the partials (fp32: the unrounded sums of tf_qlinear_partial; or T).
+template <typename T, typename TW, typename P, int VPT>
 __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, const T* __restrict__ residual,
                                                               const TW* __restrict__ weight, T* __restrict__ normed,
                                                               T* __restrict__ summed) {
@@ -118,13 +134,13 @@ __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, co
       const int col = c0 + 8 * (threadIdx.x + v * kThreads);
       if (col < a.n) {
         // issue the loads of up to 8 peers before using any (NVLink latency)
-        const int64_t off = a.offset + (row * a.n + col) * (int64_t)sizeof(T);
+        const int64_t off = a.offset + (row * a.n + col) * (int64_t)sizeof(P);
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int p0 = 0; p0 < a.world; p0 += 8) {
-          V8<T> part[8];
+          Part8<P> part[8];
 #pragma unroll
           for (int p = 0; p < 8; ++p)
-            if (p0 + p < a.world) part[p].raw = ld_peer(reinterpret_cast<const uint8_t*>(a.bufs[p0 + p]) + off);
+            if (p0 + p < a.world) part[p].load(reinterpret_cast<const uint8_t*>(a.bufs[p0 + p]) + off);
 #pragma unroll
           for (int p = 0; p < 8; ++p)
             if (p0 + p < a.world)
@@ -191,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) ar_rmsnorm_kernel(const ArArgs a, co
   }
 }
 
-template <typename T, typename TW>
+template <typename T, typename TW, typename P>
 int launch_ar(const ArArgs& a, const void* residual, const void* weight, void* normed, void* summed, int64_t m,
               cudaStream_t st) {
   const T* r = static_cast<const T*>(residual);
@@ -201,11 +217,11 @@ int launch_ar(const ArArgs& a, const void* residual, const void* weight, void* n
   // a cluster of up to 8 CTAs per row, each 128 threads x 8 columns x VPT
   if (a.n <= 8 * 8 * kThreads) {
     const unsigned c = (unsigned)cdiv(a.n, 8 * kThreads);
-    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 1>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
+    return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, P, 1>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
                      dim3(1, c, 1), a, r, w, no, su);
   }
   const unsigned c = (unsigned)cdiv(a.n, 2 * 8 * kThreads);
-  return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, 2>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
+  return launch_ex("allreduce_rmsnorm", ar_rmsnorm_kernel<T, TW, P, 2>, dim3((unsigned)m, c), dim3(kThreads), 0, st,
                    dim3(1, c, 1), a, r, w, no, su);
 }
 
@@ -216,7 +232,7 @@ extern "C" int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const
                                              int64_t offset_bytes, int32_t pad_slot, int32_t rank, int32_t world,
                                              uint32_t* counters, const void* residual, const void* weight,
                                              int w_dtype, void* normed, void* summed, int64_t M, int64_t N, float eps,
-                                             int dtype, int* error_word, void* stream) {
+                                             int dtype, int partial_dtype, int* error_word, void* stream) {
   using namespace tf;
   if (M < 0 || N < 0 || world < 1 || rank < 0 || rank >= world || pad_slot < 0 || offset_bytes < 0)
     return fail(TF_ERR_BAD_SHAPE, "allreduce_rmsnorm: bad shape or rank");
@@ -239,12 +255,26 @@ extern "C" int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const
   a.n = (int)N;
   a.eps = eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TF_BF16) {
-    if (w_dtype == TF_BF16) return launch_ar<__nv_bfloat16, __nv_bfloat16>(a, residual, weight, normed, summed, M, st);
-    if (w_dtype == TF_F16) return launch_ar<__nv_bfloat16, __half>(a, residual, weight, normed, summed, M, st);
-  } else if (dtype == TF_F16) {
-    if (w_dtype == TF_F16) return launch_ar<__half, __half>(a, residual, weight, normed, summed, M, st);
-    if (w_dtype == TF_BF16) return launch_ar<__half, __nv_bfloat16>(a, residual, weight, normed, summed, M, st);
+  if (partial_dtype == TF_F32) {
+    if (offset_bytes % 32) return fail(TF_ERR_UNALIGNED, "allreduce_rmsnorm: fp32 partials need 32-byte offsets");
+    if (dtype == TF_BF16 && w_dtype == TF_BF16)
+      return launch_ar<__nv_bfloat16, __nv_bfloat16, float>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_BF16 && w_dtype == TF_F16)
+      return launch_ar<__nv_bfloat16, __half, float>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_F16 && w_dtype == TF_F16)
+      return launch_ar<__half, __half, float>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_F16 && w_dtype == TF_BF16)
+      return launch_ar<__half, __nv_bfloat16, float>(a, residual, weight, normed, summed, M, st);
+  } else if (partial_dtype == dtype) {
+    if (dtype == TF_BF16 && w_dtype == TF_BF16)
+      return launch_ar<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_BF16 && w_dtype == TF_F16)
+      return launch_ar<__nv_bfloat16, __half, __nv_bfloat16>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_F16 && w_dtype == TF_F16)
+      return launch_ar<__half, __half, __half>(a, residual, weight, normed, summed, M, st);
+    if (dtype == TF_F16 && w_dtype == TF_BF16)
+      return launch_ar<__half, __nv_bfloat16, __half>(a, residual, weight, normed, summed, M, st);
   }
-  return fail(TF_ERR_BAD_DTYPE, "allreduce_rmsnorm: unsupported dtypes %d / %d", dtype, w_dtype);
+  return fail(TF_ERR_BAD_DTYPE, "allreduce_rmsnorm: unsupported dtypes %d / %d / partials %d", dtype, w_dtype,
+              partial_dtype);
 }

@@ -111,7 +111,7 @@ int encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void
 
 extern "C" {
 
-int tf_abi_version(void) { return 1; }
+int tf_abi_version(void) { return 2; }
 
 const char* tf_status_string(int status) {
   switch (status) {

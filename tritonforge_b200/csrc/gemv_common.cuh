@@ -25,11 +25,26 @@ struct Args {
   int swiglu;           // columns are [gate 64 | up 64] per CTA: store round(silu(g) * u), 64 wide
   uint32_t idesc;       // tcgen05 instruction descriptor (tcgen05 kernel)
   const uint8_t* wtiles;  // tiled column-major weights (tcgen05 kernel)
+  int out_f32;          // out is fp32: the unrounded sums (a row-parallel partial, no bias)
 };
 
-// round(round(v) + bias) for 4 consecutive columns, stored to out[m, col..col+3]
+// round(round(v) + bias) for 4 consecutive columns, stored to out[m, col..col+3];
+// with out_f32 the fp32 sums themselves (a tensor-parallel partial that the
+// all-reduce adds and rounds once, as a single GPU rounds its full sum)
 template <typename XT>
 __device__ __forceinline__ void finalize4(const Args& a, int m, int col, float4 v) {
+  if (a.out_f32) {
+    float* dst = static_cast<float*>(a.out) + (int64_t)m * a.ldo + col;
+    if (aligned(dst, 16)) {
+      *reinterpret_cast<float4*>(dst) = v;
+    } else {
+      dst[0] = v.x;
+      dst[1] = v.y;
+      dst[2] = v.z;
+      dst[3] = v.w;
+    }
+    return;
+  }
   float r[4] = {v.x, v.y, v.z, v.w};
   __align__(8) XT o[4];
 #pragma unroll

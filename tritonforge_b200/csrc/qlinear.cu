@@ -146,3 +146,32 @@ extern "C" int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, con
     return fail(TF_ERR_UNSUPPORTED, "qlinear_cm_swiglu: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
   return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream), true);
 }
+
+extern "C" int tf_qlinear_partial(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
+                                  const void* zeros, int param_dtype, float* out, int64_t ldo, int64_t M, int64_t N,
+                                  int64_t K, int64_t K_pad, int32_t group_size, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,     x_dtype, packed, scales, zeros, param_dtype, nullptr, 0, out, ldo,
+                    M,    N,       K,       K_pad,  group_size, workspace, workspace_bytes, 1};
+  int rc = validate(pb);
+  if (rc != TF_OK || M == 0 || N == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (gemv_supported(pb)) return gemv_launch(pb, st);
+  if (gemm_supported(pb)) return gemm_launch(pb, st);
+  return simt_launch(pb, st);
+}
+
+extern "C" int tf_qlinear_cm_partial(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm,
+                                     const void* scales, const void* zeros, int param_dtype, float* out, int64_t ldo,
+                                     int64_t M, int64_t N, int64_t K, int64_t K_pad, int32_t group_size,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace tf;
+  QLinearProblem pb{x,    ldx,     x_dtype, packed_cm, scales, zeros, param_dtype, nullptr, 0, out, ldo,
+                    M,    N,       K,       K_pad,     group_size, workspace, workspace_bytes, 1};
+  int rc = validate(pb);
+  if (rc != TF_OK || M == 0 || N == 0) return rc;
+  if (!gemv_cm_supported(pb))
+    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm_partial: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
+  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream));
+}

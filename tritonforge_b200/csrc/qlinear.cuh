@@ -25,6 +25,10 @@ struct QLinearProblem {
   int group_size;
   void* workspace;
   size_t workspace_bytes;
+  // out is fp32 and receives the unrounded fp32 sums (no bias): the partial
+  // of a row-parallel tensor-parallel projection, added across ranks and
+  // rounded once by the all-reduce
+  int out_f32;
 };
 
 bool gemv_supported(const QLinearProblem& pb);

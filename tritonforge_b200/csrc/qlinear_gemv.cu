@@ -629,6 +629,7 @@ int gemv_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu) {
   a.bias_dtype = pb.bias_dtype;
   a.out = pb.out;
   a.ldo = pb.ldo;
+  a.out_f32 = pb.out_f32;
   a.err = reinterpret_cast<int*>(pb.workspace);
   a.M = (int)pb.M;
   a.N = (int)pb.N;

@@ -22,6 +22,12 @@
 // whose workspace (tf_qlinear_workspace_bytes) is larger than the array are
 // rejected with TF_ERR_WORKSPACE. Nothing here calls cudaMalloc, cudaFree or
 // any allocating library routine.
+//
+// Word 0 of the array is the error word of the kernels' bounded waits, as in a
+// caller's workspace: a wait that gives up (after 1 s) sets a bit there and the
+// call still returns TF_OK. tf_qlinear_noalloc_error reads that word (and
+// clears it on request), so a caller without a workspace of its own can still
+// see whether any call since the last clear was cut short.
 #include <mutex>
 
 #include "qlinear.cuh"
@@ -40,8 +46,14 @@ void* g_noalloc_ptr[kMaxDevices] = {nullptr};
 // Device address of the scratch array on the current device (set up once).
 int noalloc_scratch(void** out, cudaStream_t st) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return check_launch("qlinear_noalloc: cudaGetDevice");
+  const cudaError_t ge = cudaGetDevice(&dev);
+  if (ge != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TF_ERR_CUDA, "qlinear_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(ge));
+  }
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(TF_ERR_UNSUPPORTED, "qlinear_noalloc: device %d is beyond the %d devices this library tracks", dev,
+                kMaxDevices);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
@@ -81,4 +93,20 @@ extern "C" int tf_qlinear_noalloc(const void* x, int64_t ldx, int x_dtype, const
   if (rc != TF_OK) return rc;
   return tf_qlinear(x, ldx, x_dtype, packed, scales, zeros, param_dtype, bias, bias_dtype, out, ldo, M, N, K,
                     K_pad, group_size, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int tf_qlinear_noalloc_error(int* error_out, int clear, void* stream) {
+  using namespace tf;
+  if (!error_out) return fail(TF_ERR_BAD_ARG, "qlinear_noalloc_error: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch, st);
+  if (rc != TF_OK) return rc;
+  if (cudaMemcpyAsync(error_out, scratch, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return check_launch("qlinear_noalloc_error copy");
+  if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("qlinear_noalloc_error sync");
+  if (clear && *error_out) {
+    if (cudaMemsetAsync(scratch, 0, sizeof(int), st) != cudaSuccess) return check_launch("qlinear_noalloc_error clear");
+  }
+  return *error_out ? TF_ERR_TIMEOUT : TF_OK;
 }

@@ -57,6 +57,13 @@ __global__ void __launch_bounds__(kCols) qlinear_simt_kernel(QLinearProblem pb) 
     }
   }
   if (n >= pb.N) return;
+  if (pb.out_f32) {
+    float* outf = static_cast<float*>(pb.out);
+#pragma unroll
+    for (int r = 0; r < kRowsM; ++r)
+      if (m0 + r < pb.M) outf[(m0 + r) * pb.ldo + n] = acc[r];
+    return;
+  }
   XT* out = static_cast<XT*>(pb.out);
 #pragma unroll
   for (int r = 0; r < kRowsM; ++r) {

@@ -61,6 +61,7 @@ struct Args {
   int group_size;
   int bias_dtype;
   uint32_t idesc;      // tcgen05 instruction descriptor
+  int out_f32;         // store the fp32 sums unrounded (a row-parallel partial, no bias)
 };
 
 template <typename T> struct Deq;
@@ -265,7 +266,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cc = 0; cc < kN; cc += 32) {
           uint32_t r[32];
           tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + t * kN + cc, r);
-          if (m < args.M) {
+          if (m < args.M && args.out_f32) {
+            float* dst = static_cast<float*>(args.out) + (int64_t)m * args.ldo + n0 + cc;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (n0 + cc + e < args.N) dst[e] = __uint_as_float(r[e]);
+          } else if (m < args.M) {
             XT* dst = static_cast<XT*>(args.out) + (int64_t)m * args.ldo + n0 + cc;
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
@@ -354,6 +360,7 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   a.bias_dtype = pb.bias_dtype;
   a.out = pb.out;
   a.ldo = pb.ldo;
+  a.out_f32 = pb.out_f32;
   a.err = reinterpret_cast<int*>(pb.workspace);
   a.M = (int)pb.M;
   a.N = (int)pb.N;

@@ -22,8 +22,11 @@ rmsnorm_residual (same rounding). q|k|v are the reference's separate
 QuantLinear tensors concatenated along N and gate|up interleaved per 64
 columns, which changes no value: the fused gate|up kernel rounds each
 projection to the model dtype before the SwiGLU, as the reference's separate
-launches do. With a tensor-parallel group the o_proj / down_proj all-reduce is
-fused with the following rmsnorm_residual (tf_allreduce_rmsnorm_residual).
+launches do. With a tensor-parallel group, o_proj / down_proj leave each
+rank's unrounded fp32 partial sum (tf_qlinear_partial); the partials are added
+across ranks in fp32 and rounded once, fused with the following
+rmsnorm_residual (tf_allreduce_rmsnorm_residual over peer memory, or an NCCL
+fp32 all-reduce), so a sharded layer rounds where the single-GPU layer rounds.
 
 The prompt is prefilled through the patched transformers model itself and its
 KV cache copied into the static cache.
@@ -216,18 +219,20 @@ class QwenWeights:
             out.append(d)
         return out
 
-    def save(self, path: str) -> None:
-        """Write these (K-major) weights to a directory: see shard_cache."""
+    def save(self, path: str, tp: int = 1, rank: int = 0) -> None:
+        """Write these (K-major) weights, rank `rank` of a `tp`-way shard, to a
+        directory: see shard_cache."""
         from .shard_cache import save_weights
 
-        save_weights(self, path)
+        save_weights(self, path, tp, rank)
 
     @classmethod
-    def load(cls, path: str, device=None) -> "QwenWeights":
-        """Weights written by `save`, on `device` (default: current CUDA device)."""
+    def load(cls, path: str, device=None, tp: int | None = None, rank: int | None = None) -> "QwenWeights":
+        """Weights written by `save`, on `device` (default: current CUDA
+        device); with `tp`/`rank`, a shard of another degree or rank is refused."""
         from .shard_cache import load_weights
 
-        return load_weights(path, device)
+        return load_weights(path, device, tp, rank)
 
     def to_colmajor(self, min_k: int = 2048) -> "QwenWeights":
         """`colmajor_layers` in place: the K-major packed tensors are dropped
@@ -365,8 +370,15 @@ class QwenDecoder:
             "mlp": torch.empty(B, self.H, dtype=dt, device=dev),
             "logits": torch.empty(B, self.lm_head.shape[0], dtype=dt, device=dev),
         }
+        # Tensor parallel: o_proj / down_proj leave unrounded fp32 partial sums
+        # (tf_qlinear_partial), added across ranks in fp32 and rounded once, so
+        # a sharded layer rounds exactly where the single-GPU layer does.
+        self.tp = group is not None
         if self.fused_allreduce:
             self._setup_symmetric(B)
+        elif self.tp:
+            self.buf["o_part"] = torch.empty(B, self.H, dtype=torch.float32, device=dev)
+            self.buf["mlp_part"] = torch.empty(B, self.H, dtype=torch.float32, device=dev)
         if self.vocab_parallel:
             self.buf["best"] = torch.empty(B, 2, dtype=torch.float32, device=dev)     # (logit, token id)
             self.buf["all_best"] = torch.empty(self.world, B, 2, dtype=torch.float32, device=dev)
@@ -379,27 +391,26 @@ class QwenDecoder:
     PAD_SLOT = 64  # first signal-pad slot this decoder uses
 
     def _setup_symmetric(self, B: int) -> None:
-        """Symmetric buffer holding the o_proj and down_proj partial tiles
-        (they alternate, which makes buffer reuse safe without a second
+        """Symmetric buffer holding the o_proj and down_proj fp32 partial
+        tiles (they alternate, which makes buffer reuse safe without a second
         barrier), peer pointers and signal pads (torch symmetric memory)."""
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
 
         n = B * self.H
-        gname = self.group.group_name
-        if hasattr(symm, "is_symm_mem_enabled_for_group") and not symm.is_symm_mem_enabled_for_group(gname):
-            symm.enable_symm_mem_for_group(gname)
-        sbuf = symm.empty(2 * n, dtype=self.dtype, device=self.dev)
+        sbuf = symm.empty(2 * n, dtype=torch.float32, device=self.dev)
         hdl = symm.rendezvous(sbuf, self.group)
         if hdl.signal_pad_size < 4 * (self.PAD_SLOT + self.world):
             raise RuntimeError("symmetric-memory signal pad too small")
         hdl.get_signal_pad(hdl.rank, (self.PAD_SLOT + self.world,), torch.int32)[self.PAD_SLOT:].zero_()
         self._symm = (sbuf, hdl)
-        self.buf["o"] = sbuf[:n].view(B, self.H)
-        self.buf["mlp"] = sbuf[n:].view(B, self.H)
+        self.buf["o_part"] = sbuf[:n].view(B, self.H)
+        self.buf["mlp_part"] = sbuf[n:].view(B, self.H)
         esz = sbuf.element_size()
         base = int(hdl.offset)  # this tensor's offset inside every rank's buffer
         self._ar_off = {"o": base, "mlp": base + n * esz}
+        if any(off % 32 for off in self._ar_off.values()):
+            raise RuntimeError(f"symmetric partial tiles not 32-byte aligned: {self._ar_off}")
         self._ar_ctr = torch.zeros(2, dtype=torch.int32, device=self.dev)
         self._ar_err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         torch.cuda.synchronize(self.dev)
@@ -411,18 +422,59 @@ class QwenDecoder:
         _lib.check(self._lib.tf_allreduce_rmsnorm_residual(
             hdl.buffer_ptrs_dev, hdl.signal_pad_ptrs_dev, self._ar_off[which], self.PAD_SLOT, self.rank, self.world,
             self._ar_ctr.data_ptr(), res.data_ptr(), weight.data_ptr(), _lib.dtype_code(weight.dtype),
-            normed.data_ptr(), summed.data_ptr(), self.B, self.H, self.eps, self._dt, self._ar_err.data_ptr(),
-            _lib.stream_ptr(self.dev)), "allreduce_rmsnorm_residual")
+            normed.data_ptr(), summed.data_ptr(), self.B, self.H, self.eps, self._dt, _lib.F32,
+            self._ar_err.data_ptr(), _lib.stream_ptr(self.dev)), "allreduce_rmsnorm_residual")
 
     def allreduce_errors(self) -> int:
         """Device error bits of the fused all-reduce (16: a peer's signal did not arrive within 1 s)."""
         return int(self._ar_err.item()) if self.fused_allreduce else 0
+
+    def device_errors(self) -> int:
+        """Error bits the decode kernels left on this device: the fused
+        all-reduce's word and the int4 kernels' workspace words (a bounded
+        wait that gave up after 1 s). 0 means every launch ran to the end;
+        anything else means the outputs of some step are not to be trusted."""
+        return self.allreduce_errors() | _lib.workspaces.errors(self.dev)
 
     # ------------------------------------------------------------------ step
     def _lin(self, x: torch.Tensor, ql, out: torch.Tensor) -> torch.Tensor:
         if isinstance(ql, CMLinear):
             return ql(x, out=out)
         return kernels.quantized_linear(x, ql.packed, ql.scales, ql.zeros, ql.bias, ql.group_size, out=out)
+
+    def _lin_partial(self, x: torch.Tensor, ql, out: torch.Tensor) -> None:
+        """out (fp32) = x @ W unrounded, no bias: this rank's share of a
+        row-parallel projection (tf_qlinear_partial / tf_qlinear_cm_partial)."""
+        m, k = x.shape
+        cm = isinstance(ql, CMLinear)
+        kp = ql.scales.shape[0] * ql.group_size
+        n = ql.scales.shape[1]
+        ws = _lib.workspaces.get(self.dev, 256)
+        fn = self._lib.tf_qlinear_cm_partial if cm else self._lib.tf_qlinear_partial
+        _lib.check(fn(x.data_ptr(), x.stride(0), self._dt, (ql.tiles if cm else ql.packed).data_ptr(),
+                      ql.scales.data_ptr(), ql.zeros.data_ptr(), _lib.dtype_code(ql.scales.dtype), out.data_ptr(),
+                      out.stride(0), m, n, k, kp, ql.group_size, ws.data_ptr(), ws.numel(),
+                      _lib.stream_ptr(self.dev)), "qlinear_partial")
+
+    def _row_parallel(self, x: torch.Tensor, ql, which: str, res: torch.Tensor, weight: torch.Tensor,
+                      normed: torch.Tensor, summed: torch.Tensor) -> None:
+        """o_proj / down_proj followed by the residual add and the next RMSNorm.
+        Single GPU: the projection rounds its own output. Tensor parallel: an
+        fp32 partial per rank, summed across ranks in fp32 (the fused peer-memory
+        kernel, or an NCCL all-reduce), rounded once, then residual + RMSNorm."""
+        b = self.buf
+        if not self.tp:
+            self._lin(x, ql, b[which])
+            kernels.rmsnorm_residual(b[which], res, weight, self.eps, out=(normed, summed))
+            return
+        part = b[which + "_part"]
+        self._lin_partial(x, ql, part)
+        if self.fused_allreduce:
+            self._ar_norm(which, res, weight, normed, summed)
+            return
+        self._all_reduce(part)
+        b[which].copy_(part)  # one rounding of the fp32 sum
+        kernels.rmsnorm_residual(b[which], res, weight, self.eps, out=(normed, summed))
 
     def _all_reduce(self, t: torch.Tensor) -> None:
         if self.group is None:
@@ -444,36 +496,23 @@ class QwenDecoder:
         res, res_next = b["res_a"], b["res_b"]
         posp = self.pos.data_ptr()
         lenp = posp + 4
+        nl = len(self.layers)
         for li, L in enumerate(self.layers):
             if li == 0:
                 kernels.rmsnorm(b["x"], L["in_norm"], self.eps, out=b["normed"])
                 res.copy_(b["x"])
-            else:
-                if self.fused_allreduce:
-                    self._ar_norm("mlp", res, L["in_norm"], b["normed"], res_next)
-                else:
-                    kernels.rmsnorm_residual(b["mlp"], res, L["in_norm"], self.eps, out=(b["normed"], res_next))
-                res, res_next = res_next, res
             self._lin(b["normed"], L["qkv"], b["qkv"])
             _lib.check(lib.tf_decode_attention_rope(
                 b["qkv"].data_ptr(), b["qkv"].stride(0), self.cos.data_ptr(), self.sin.data_ptr(),
                 self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), posp, b["attn"].data_ptr(), self.B,
                 self.Hq, self.Hkv, self.D, self.T, self.scale, self._dt, st), "decode_attention_rope")
-            self._lin(b["attn"], L["o"], b["o"])
-            if self.fused_allreduce:
-                self._ar_norm("o", res, L["post_norm"], b["normed"], res_next)
-            else:
-                self._all_reduce(b["o"])
-                kernels.rmsnorm_residual(b["o"], res, L["post_norm"], self.eps, out=(b["normed"], res_next))
+            self._row_parallel(b["attn"], L["o"], "o", res, L["post_norm"], b["normed"], res_next)
             res, res_next = res_next, res
             self._gate_up(b["normed"], L["gu"], b["act"])
-            self._lin(b["act"], L["down"], b["mlp"])
-            if not self.fused_allreduce:
-                self._all_reduce(b["mlp"])
-        if self.fused_allreduce:
-            self._ar_norm("mlp", res, self.final_norm, b["normed"], res_next)
-        else:
-            kernels.rmsnorm_residual(b["mlp"], res, self.final_norm, self.eps, out=(b["normed"], res_next))
+            # the next layer's input norm, or the final norm after the last layer
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < nl else self.final_norm
+            self._row_parallel(b["act"], L["down"], "mlp", res, nxt, b["normed"], res_next)
+            res, res_next = res_next, res
         torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
         if self.vocab_parallel:
             self._vocab_parallel_argmax()
@@ -619,3 +658,65 @@ def _layer_kv(cache, li: int):
     if hasattr(cache, "key_cache"):
         return cache.key_cache[li], cache.value_cache[li]
     return cache[li][0], cache[li][1]
+
+
+@torch.no_grad()
+def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, seed: int = 7,
+              context: int = 40) -> dict:
+    """Tensor-parallel decode against a single-GPU decode of the same weights.
+
+    Every rank builds the same full `layers`-layer weights of the Qwen2.5
+    shape `name` (seeded), decodes them alone (tp=1) and decodes its own shard
+    with the group (the engine's tensor-parallel path, fused all-reduce), both
+    from the same random KV cache of `context` positions, for `steps` greedy
+    steps fed the same tokens. Returns max |logits_tp - logits_tp1| / RMS over
+    all steps and ranks' vocabulary slices, whether the greedy tokens agree,
+    the largest reference top-2 gap among rows whose tokens differ (a genuine
+    near-tie when within 2e-2 x RMS), whether all ranks produced the same
+    tokens, and the device error bits of both decoders."""
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=seed, layers=layers)
+    t_max = context + steps + 8
+    ref = QwenDecoder(full, batch, t_max)
+    ref.fill_cache(context, seed=seed + 1)
+    dec = QwenDecoder(full.shard(world, rank), batch, t_max, group=group)
+    h = dec.Hkv
+    dec.k_cache.copy_(ref.k_cache[:, :, rank * h:(rank + 1) * h])
+    dec.v_cache.copy_(ref.v_cache[:, :, rank * h:(rank + 1) * h])
+    dec.tokens.copy_(ref.tokens)
+    dec.pos.copy_(ref.pos)
+    dec.capture()
+    v0, nv = dec.v0, dec.lm_head.shape[0]
+    worst, same, tie_gap, ranks_same = 0.0, True, 0.0, True
+    for _ in range(steps):
+        ref.step()
+        dec.graph.replay()
+        want = ref.buf["logits"][:, v0:v0 + nv].float()
+        rms = float(ref.buf["logits"].float().pow(2).mean().sqrt())
+        worst = max(worst, float((dec.buf["logits"].float() - want).abs().max()) / rms)
+        diff = (dec.tokens != ref.tokens).nonzero().flatten()
+        if diff.numel():
+            same = False
+            r32 = ref.buf["logits"].float()
+            gap = float((r32[diff, ref.tokens[diff]] - r32[diff, dec.tokens[diff]]).max()) / rms
+            tie_gap = max(tie_gap, gap)
+        gathered = [torch.empty_like(dec.tokens) for _ in range(world)]
+        dist.all_gather(gathered, dec.tokens, group=group)
+        ranks_same &= all(torch.equal(gathered[0], t) for t in gathered)
+        dec.tokens.copy_(ref.tokens)  # both decodes continue from the same tokens
+    errs = dec.device_errors() | ref.device_errors()
+    stats = torch.tensor([worst, 0.0 if same else 1.0, tie_gap, 0.0 if ranks_same else 1.0, float(errs)],
+                         dtype=torch.float64, device=dev)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
+    dec.release()
+    del dec, ref, full
+    torch.cuda.empty_cache()
+    return {"model": name, "layers": layers, "steps": steps, "batch": batch, "context": context,
+            "max_err_over_rms": float(stats[0]), "tokens_equal": stats[1].item() == 0.0,
+            "near_tie_gap_over_rms": float(stats[2]), "ranks_identical": stats[3].item() == 0.0,
+            "device_errors": int(stats[4]), "tolerance": 2e-2,
+            "ok": float(stats[0]) <= 2e-2 and float(stats[2]) <= 2e-2 and stats[3].item() == 0.0
+            and int(stats[4]) == 0}

@@ -7,9 +7,15 @@ stored in the reference's own formats — packed uint8 [K_pad/2, N] K-major,
 scales and zeros [K_pad/g, N], bias [N] — one rank's tensor-parallel shard
 per directory:
 
-    <dir>/manifest.json   format tag, decoder shape, tensor table
+    <dir>/manifest.json   format tag, decoder shape, tensor-parallel degree
+                          and rank, the layout of the fused projections,
+                          the size of tensors.bin, tensor table
     <dir>/tensors.bin     the tensors' raw little-endian bytes, each at a
                           256-byte-aligned offset
+
+Both files are written under temporary names and renamed (blob first); the
+manifest records the blob's size, so a blob that does not belong to its
+manifest (an interrupted save) fails the load instead of loading.
 
 Raw bytes plus a JSON table keep the files readable without Python (a host
 runtime can memory-map tensors.bin and take offsets from the manifest). A
@@ -24,7 +30,10 @@ import os
 import numpy as np
 import torch
 
-FORMAT = "tritonforge_b200-int4-shard/1"
+FORMAT = "tritonforge_b200-int4-shard/2"
+# how the decoder's fused projections are laid out (checked on load)
+LAYOUT = {"qkv": "q|k|v projections concatenated along N (q heads, then k, then v)",
+          "gu": "gate|up interleaved per 64 columns: [gate 0:64 | up 0:64 | gate 64:128 | ...]"}
 _ALIGN = 256
 _DTYPES = {torch.uint8: ("u8", np.uint8), torch.float16: ("f16", np.uint16), torch.bfloat16: ("bf16", np.uint16),
            torch.float32: ("f32", np.float32), torch.int32: ("i32", np.int32)}
@@ -41,9 +50,10 @@ def _to_bytes(t: torch.Tensor) -> bytes:
     return a.numpy().view(npdt).tobytes()
 
 
-def save_weights(w, path: str) -> None:
-    """Write `w` (a QwenWeights whose projections are K-major QuantLinear) to
-    the directory `path` (created if needed; existing files are replaced)."""
+def save_weights(w, path: str, tp: int = 1, rank: int = 0) -> None:
+    """Write `w` (rank `rank` of a `tp`-way tensor-parallel shard, as a
+    QwenWeights whose projections are K-major QuantLinear) to the directory
+    `path` (created if needed; existing files are replaced)."""
     from .integration.qwen import QuantLinear
 
     os.makedirs(path, exist_ok=True)
@@ -80,17 +90,22 @@ def save_weights(w, path: str) -> None:
         if not tied:
             put("lm_head", w.lm_head)
         put("final_norm", w.final_norm)
-    manifest = {"format": FORMAT, "layers": len(w.layers), "tied_lm_head": bool(tied),
+    manifest = {"format": FORMAT, "tp": int(tp), "rank": int(rank), "layout": LAYOUT,
+                "blob_bytes": os.path.getsize(tmp), "layers": len(w.layers), "tied_lm_head": bool(tied),
                 "config": {k: getattr(w, k) for k in _FIELDS}, "linears": linears, "tensors": table}
-    os.replace(tmp, os.path.join(path, "tensors.bin"))
-    with open(os.path.join(path, "manifest.json"), "w") as f:
+    mtmp = os.path.join(path, "manifest.json.tmp")
+    with open(mtmp, "w") as f:
         json.dump(manifest, f, indent=1)
+    os.replace(tmp, os.path.join(path, "tensors.bin"))
+    os.replace(mtmp, os.path.join(path, "manifest.json"))
 
 
-def load_weights(path: str, device=None):
+def load_weights(path: str, device=None, tp: int | None = None, rank: int | None = None):
     """Read a directory written by `save_weights` into a QwenWeights on
     `device` (default: the current CUDA device). Raises ValueError for a
-    directory of another format or truncated data."""
+    directory of another format or layout, a blob that does not match its
+    manifest, truncated data, or a shard of another tensor-parallel degree or
+    rank than `tp` / `rank` (when given)."""
     from .decode import QwenWeights
     from .integration.qwen import QuantLinear
 
@@ -98,6 +113,12 @@ def load_weights(path: str, device=None):
         man = json.load(f)
     if man.get("format") != FORMAT:
         raise ValueError(f"{path}: not a {FORMAT} directory (format {man.get('format')!r})")
+    if man.get("layout") != LAYOUT:
+        raise ValueError(f"{path}: fused projections in another layout: {man.get('layout')!r}")
+    if tp is not None and man.get("tp") != tp or rank is not None and man.get("rank") != rank:
+        raise ValueError(f"{path}: shard of tp={man.get('tp')} rank={man.get('rank')}, wanted tp={tp} rank={rank}")
+    if os.path.getsize(os.path.join(path, "tensors.bin")) != man.get("blob_bytes"):
+        raise ValueError(f"{path}: tensors.bin does not match its manifest (size differs)")
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device())
     blob = np.memmap(os.path.join(path, "tensors.bin"), dtype=np.uint8, mode="r")
