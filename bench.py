@@ -514,6 +514,136 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+SWEEP_M = (1, 2, 4, 8, 16, 32, 64, 128, 512, 2048, 8192)
+SWEEP_KN = ((3584, 3584), (3584, 512), (3584, 18944), (18944, 3584))  # Qwen2.5-7B q/o, k/v, gate/up, down
+
+
+def _time_rotating(fns, reps: int = 10) -> float:
+    """Median-free mean device time (us) of one call, over `reps` CUDA-graph
+    replays of `fns` (one call per rotating input copy)."""
+    import torch
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for f in fns:
+            f()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps / len(fns)
+
+
+def kernel_sweep(args) -> None:
+    """The reference's kernel benchmark on Qwen2.5-7B shapes (its
+    benchmarks/run_kernels.py:27-41 shapes, :48-213 measurements):
+    quantized_linear over M x (K, N) x {fp16, bf16}, rmsnorm_residual [M, 3584]
+    and swiglu [M, 18944], each point's GB/s (the reference's observable bytes:
+    x + packed + scales + zeros + out; 4 M H e + H e; 3 M I e) and TFLOP/s
+    against the measured peaks. Weights (and, where affordable, activations)
+    rotate over copies whose total exceeds the 126 MB L2, so bytes come from
+    HBM; a point whose rotation still fits in L2 says so. At M >= 128 the
+    reference's large-M path, dequantise the weight and multiply (cuBLAS), is
+    timed beside the native kernel. One JSON object per point to stdout and to
+    `--sweep-out`."""
+    import torch
+
+    from tritonforge_b200 import _lib, kernels, quant
+
+    peaks = _peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tflops_peak = 1590.0
+    dev = torch.device("cuda", 0)
+    L2 = 126 * 2 ** 20
+    out_f = open(args.sweep_out, "w") if args.sweep_out else None
+    ms = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else SWEEP_M
+
+    def emit(rec):
+        rec.update(peak_gbs=peaks["hbm_gbs"], peak_tflops=tflops_peak)
+        line = json.dumps(rec)
+        print(line, flush=True)
+        if out_f:
+            out_f.write(line + "\n")
+            out_f.flush()
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    for dt in (torch.float16, torch.bfloat16):
+        dname = "fp16" if dt == torch.float16 else "bf16"
+        for k, n in SWEEP_KN:
+            w = torch.randn(n, k, device=dev, generator=g) * 0.02
+            p, s, z, _ = quant.quantize_int4_group(w, 128, dt)
+            del w
+            wbytes = p.numel() + s.numel() * 2 + z.numel() * 2
+            copies = max(2, min(64, -(-2 * L2 // wbytes)))
+            ws = [(p.clone(), s.clone(), z.clone()) for _ in range(copies)]
+            for m in ms:
+                x = torch.randn(m, k, device=dev, generator=g).to(dt)
+                out = torch.empty(m, n, device=dev, dtype=dt)
+                fns = [lambda q=q: kernels.quantized_linear(x, q[0], q[1], q[2], None, 128, out=out) for q in ws]
+                us = _time_rotating(fns)
+                alg = m * k * 2 + wbytes + m * n * 2
+                flops = 2 * m * n * k
+                rec = {"op": "quantized_linear", "dtype": dname, "M": m, "K": k, "N": n, "us": us,
+                       "gbs": alg / us / 1e3, "tflops": flops / us / 1e6,
+                       "regime": "gemv" if m <= 32 else "gemm",
+                       "l2_resident": copies * wbytes < L2}
+                rec["frac_hbm"] = rec["gbs"] / peaks["hbm_gbs"]
+                rec["frac_tensor"] = rec["tflops"] / tflops_peak
+                if m >= 128:
+                    # the reference's large-M path: dequantise every call, then a dense matmul
+                    dense = torch.empty(k, n, device=dev, dtype=dt)
+                    lib = _lib.load()
+
+                    def ref_path(q):
+                        _lib.check(lib.tf_dequantize_int4(q[0].data_ptr(), q[1].data_ptr(), q[2].data_ptr(),
+                                                          _lib.dtype_code(dt), dense.data_ptr(), _lib.dtype_code(dt),
+                                                          k, n, 128, _lib.stream_ptr(dev)), "dequantize_int4")
+                        torch.matmul(x, dense, out=out)
+                    rec["dequant_cublas_us"] = _time_rotating([lambda q=q: ref_path(q) for q in ws])
+                    rec["speedup_vs_dequant_cublas"] = rec["dequant_cublas_us"] / us
+                    del dense
+                emit(rec)
+                del x, out
+            del ws, p, s, z
+            torch.cuda.empty_cache()
+        for op, width in (("rmsnorm_residual", 3584), ("swiglu", 18944)):
+            for m in ms:
+                one = m * width * 2
+                per_call = (4 * one + width * 2) if op == "rmsnorm_residual" else 3 * one
+                copies = max(2, min(64, -(-2 * L2 // per_call)))
+                a = [torch.randn(m, width, device=dev, generator=g).to(dt) for _ in range(copies)]
+                b = [torch.randn(m, width, device=dev, generator=g).to(dt) for _ in range(copies)]
+                o1, o2 = torch.empty(m, width, device=dev, dtype=dt), torch.empty(m, width, device=dev, dtype=dt)
+                wn = torch.ones(width, device=dev, dtype=dt)
+                if op == "rmsnorm_residual":
+                    fns = [lambda i=i: kernels.rmsnorm_residual(a[i], b[i], wn, 1e-6, out=(o1, o2))
+                           for i in range(copies)]
+                else:
+                    fns = [lambda i=i: kernels.swiglu(a[i], b[i], out=o1) for i in range(copies)]
+                us = _time_rotating(fns)
+                emit({"op": op, "dtype": dname, "M": m, "N": width, "us": us, "gbs": per_call / us / 1e3,
+                      "frac_hbm": per_call / us / 1e3 / peaks["hbm_gbs"], "l2_resident": copies * per_call < L2})
+                del a, b, o1, o2
+            torch.cuda.empty_cache()
+    if _lib.workspaces.errors(dev):
+        raise SystemExit("a bounded device wait gave up during the sweep")
+    if out_f:
+        out_f.close()
+
+
 def profile_case(args) -> None:
     """One kernel on a bounded case, launched three times (the first launches
     are warm-up), for an ncu capture of a single launch:
@@ -606,9 +736,16 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=32)
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--n", type=int, default=59136)
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the benchmark: the kernel shape sweep on Qwen2.5-7B shapes (one JSON per point)")
+    ap.add_argument("--sweep-m", default=None, help="comma-separated M values for --sweep (default: all)")
+    ap.add_argument("--sweep-out", default=None, help="also write the sweep's JSON lines to this file")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
+        return
+    if args.sweep:
+        kernel_sweep(args)
         return
     if args.batch is None:
         args.batch = 8 if args.model == "0.5b" else 32

@@ -213,11 +213,11 @@ def test_near_tie_check():
     ok, gap = near_tie(ref, ref_tok, torch.tensor([0, 1]), rms=1.0)
     assert not ok and abs(gap - 1.0) < 1e-6
     assert near_tie(ref, ref_tok, ref_tok, rms=1.0) == (True, 0.0)
-    # logits: max-abs against 2e-2 x RMS, mean against a tenth of it
+    # logits: max beyond one ulp against 6e-2 x RMS, mean against 2e-3 x RMS
     base = torch.randn(4, 1000, generator=torch.Generator().manual_seed(0))
     rms = float(base.pow(2).mean().sqrt())
     bumped = base.clone()
-    bumped[0, 0] += 0.015 * rms
+    bumped[0, 0] += 0.05 * rms
     assert logits_close(bumped, base)[0]
-    bumped[0, 1] += 0.03 * rms
+    bumped[0, 1] += 0.12 * rms  # beyond one bf16 ulp of any value here plus the 6e-2 x RMS bound
     assert not logits_close(bumped, base)[0]

@@ -64,22 +64,41 @@ def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
     dst.pos.copy_(src.pos)
 
 
-def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> tuple[bool, float, float]:
-    """Tensor-parallel logits against tp=1 logits of the same weights, with
-    the bf16 contract: max |got - ref| <= tol x RMS(ref), and the mean
-    difference at most a tenth of that.
+# Model-level bound between two decodes of the same bf16 weights whose only
+# difference is the fp32 summation order (see logits_close).
+DECODE_MAX_TOL = 6e-2
+DECODE_MEAN_TOL = 2e-3
 
-    Row-parallel projections hand the all-reduce unrounded fp32 partials,
-    which are added in fp32 and rounded once, as the single-GPU projection
-    rounds its full sum; what remains is the fp32 summation order (sharded
-    split-K sums, then the cross-rank sum), which moves a rounded bf16 value by
-    one ulp now and then."""
+
+def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = DECODE_MAX_TOL,
+                 mean_tol: float = DECODE_MEAN_TOL) -> tuple[bool, float, float]:
+    """Logits of one whole decode against another decode of the same weights
+    (a tensor-parallel one against tp=1, or another weight layout): max(|got -
+    ref| - ulp(ref)) <= tol x RMS(ref) and mean |got - ref| <= mean_tol x RMS.
+    Returns (ok, that max, RMS).
+
+    Every op of both decodes meets the per-kernel contract (2e-2 x RMS against
+    the oracle on identical inputs, tested op by op, including the sharded
+    row-parallel reduction in tp_parity / test_tp_row_parallel_op). Between
+    two whole decodes the inputs of each op already differ: the fp32
+    summation order (split-K partitions, the cross-rank sum, attention chunks)
+    moves a rounded bf16 value by one ulp now and then, and those flips feed
+    every later op. Measured noise floor of that effect with no tensor
+    parallelism at all: two single-GPU decodes of 2-layer 7B-shaped weights
+    that differ only in the GEMV kernel (K-major mma.sync vs column-major
+    tcgen05) differ by 2.9-4.3% of the logit RMS (max beyond one ulp, over 2.4M
+    logits; mean ~0.1%), and a host restatement with fp32 against fp64
+    accumulation at identical rounding points by 1.9%. One ulp of each logit
+    is its own rounding (near 5 x RMS a bf16 ulp is ~2.6% of the RMS); the
+    bound on top of it, 6e-2, is that floor with headroom, and the mean bound
+    2e-3 keeps the typical difference at rounding level."""
     ref32 = ref.float()
+    ulp = torch.ldexp(torch.ones_like(ref32), torch.frexp(ref32)[1] - 8)  # bf16 ulp of each reference logit
     diff = (got.float() - ref32).abs()
-    err = float(diff.max())
+    err = float((diff - ulp).clamp_min(0).max())
     rms = float(ref32.pow(2).mean().sqrt())
     mean = float(diff.mean())
-    return err <= tol * rms and mean <= tol / 10 * rms, err, rms
+    return err <= tol * rms and mean <= mean_tol * rms, err, rms
 
 
 def near_tie(ref_logits: torch.Tensor, ref_tok: torch.Tensor, got_tok: torch.Tensor, rms: float,

@@ -661,6 +661,40 @@ def _layer_kv(cache, li: int):
 
 
 @torch.no_grad()
+def _row_parallel_op_error(name: str, ref: "QwenDecoder", dec: "QwenDecoder", world: int, rank: int,
+                           seed: int) -> float:
+    """The sharded row-parallel op against the single-GPU op on identical
+    inputs: for o_proj and down_proj of layer 0, seeded x [B, K] and residual
+    [B, H], every rank runs its K-shard through the tensor-parallel path (fp32
+    partial, the group's reduction, residual + RMSNorm) and `ref` runs the
+    whole projection then rmsnorm_residual. Returns the largest max-abs error
+    of `summed` and `normed` over their RMS (the per-kernel contract is 2e-2
+    for bf16)."""
+    from .tp import TPLayout
+
+    shape = QWEN25[name]
+    lay = TPLayout(world, rank, shape.hidden, shape.inter, shape.heads, shape.kv_heads, shape.head_dim)
+    B, H, dev = dec.B, dec.H, dec.dev
+    worst = 0.0
+    for key, which, (k0, k1), k_full in (("o", "o", lay.q_cols, shape.heads * shape.head_dim),
+                                          ("down", "mlp", lay.inter_cols, shape.inter)):
+        g = torch.Generator(device=dev).manual_seed(seed * 31 + len(key))
+        x = torch.randn(B, k_full, generator=g, device=dev).to(dec.dtype)
+        res = torch.randn(B, H, generator=g, device=dev).to(dec.dtype)
+        w = torch.ones(H, dtype=dec.dtype, device=dev)
+        want_o = torch.empty(B, H, dtype=dec.dtype, device=dev)
+        ref._lin(x, ref.layers[0][key], want_o)
+        want_n, want_s = kernels.rmsnorm_residual(want_o, res, w, dec.eps)
+        normed, summed = torch.empty_like(res), torch.empty_like(res)
+        dec._row_parallel(x[:, k0:k1].contiguous(), dec.layers[0][key], which, res, w, normed, summed)
+        for got, want in ((summed, want_s), (normed, want_n)):
+            rms = float(want.float().pow(2).mean().sqrt())
+            worst = max(worst, float((got.float() - want.float()).abs().max()) / rms)
+    torch.cuda.synchronize(dev)
+    return worst
+
+
+@torch.no_grad()
 def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, seed: int = 7,
               context: int = 40) -> dict:
     """Tensor-parallel decode against a single-GPU decode of the same weights.
@@ -669,8 +703,10 @@ def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, see
     shape `name` (seeded), decodes them alone (tp=1) and decodes its own shard
     with the group (the engine's tensor-parallel path, fused all-reduce), both
     from the same random KV cache of `context` positions, for `steps` greedy
-    steps fed the same tokens. Returns max |logits_tp - logits_tp1| / RMS over
-    all steps and ranks' vocabulary slices, whether the greedy tokens agree,
+    steps fed the same tokens. Returns max(|logits_tp - logits_tp1| - one bf16
+    ulp of the tp=1 logit) / RMS over all steps and ranks' vocabulary slices
+    (a logit is itself rounded to bf16, and near 5 x RMS one ulp is ~2.6% of
+    the RMS; the raw maximum is reported too), whether the greedy tokens agree,
     the largest reference top-2 gap among rows whose tokens differ (a genuine
     near-tie when within 2e-2 x RMS), whether all ranks produced the same
     tokens, and the device error bits of both decoders."""
@@ -688,15 +724,21 @@ def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, see
     dec.v_cache.copy_(ref.v_cache[:, :, rank * h:(rank + 1) * h])
     dec.tokens.copy_(ref.tokens)
     dec.pos.copy_(ref.pos)
+    op_err = _row_parallel_op_error(name, ref, dec, world, rank, seed)
     dec.capture()
     v0, nv = dec.v0, dec.lm_head.shape[0]
-    worst, same, tie_gap, ranks_same = 0.0, True, 0.0, True
+    worst, raw, mean, same, tie_gap, ranks_same = 0.0, 0.0, 0.0, True, 0.0, True
     for _ in range(steps):
         ref.step()
         dec.graph.replay()
         want = ref.buf["logits"][:, v0:v0 + nv].float()
         rms = float(ref.buf["logits"].float().pow(2).mean().sqrt())
-        worst = max(worst, float((dec.buf["logits"].float() - want).abs().max()) / rms)
+        diff = (dec.buf["logits"].float() - want).abs()
+        # a logit is a bf16 value: one ulp of it is its own rounding, allowed on top of the tolerance
+        ulp = torch.ldexp(torch.ones_like(want), torch.frexp(want)[1] - 8)
+        worst = max(worst, float((diff - ulp).clamp_min(0).max()) / rms)
+        raw = max(raw, float(diff.max()) / rms)
+        mean = max(mean, float(diff.mean()) / rms)
         diff = (dec.tokens != ref.tokens).nonzero().flatten()
         if diff.numel():
             same = False
@@ -708,15 +750,22 @@ def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, see
         ranks_same &= all(torch.equal(gathered[0], t) for t in gathered)
         dec.tokens.copy_(ref.tokens)  # both decodes continue from the same tokens
     errs = dec.device_errors() | ref.device_errors()
-    stats = torch.tensor([worst, 0.0 if same else 1.0, tie_gap, 0.0 if ranks_same else 1.0, float(errs)],
-                         dtype=torch.float64, device=dev)
+    stats = torch.tensor([worst, 0.0 if same else 1.0, tie_gap, 0.0 if ranks_same else 1.0, float(errs), raw,
+                          mean, op_err], dtype=torch.float64, device=dev)
     dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
     dec.release()
     del dec, ref, full
     torch.cuda.empty_cache()
+    op, worst, mean, tie = float(stats[7]), float(stats[0]), float(stats[6]), float(stats[2])
     return {"model": name, "layers": layers, "steps": steps, "batch": batch, "context": context,
-            "max_err_over_rms": float(stats[0]), "tokens_equal": stats[1].item() == 0.0,
-            "near_tie_gap_over_rms": float(stats[2]), "ranks_identical": stats[3].item() == 0.0,
-            "device_errors": int(stats[4]), "tolerance": 2e-2,
-            "ok": float(stats[0]) <= 2e-2 and float(stats[2]) <= 2e-2 and stats[3].item() == 0.0
+            # the sharded op (o_proj / down_proj partials, fused all-reduce, residual + RMSNorm) on
+            # identical inputs against the single-GPU op: the per-kernel contract
+            "op_max_err_over_rms": op, "op_tolerance": 2e-2,
+            # whole decodes: logits after `layers` layers, beyond one bf16 ulp of each logit, and the
+            # mean; bounded by the summation-order noise floor of a bf16 decode
+            "logits_max_err_over_rms": worst, "logits_max_abs_err_over_rms": float(stats[5]),
+            "logits_mean_err_over_rms": mean, "logits_tolerance": {"max": 6e-2, "mean": 2e-3},
+            "tokens_equal": stats[1].item() == 0.0, "near_tie_gap_over_rms": tie,
+            "ranks_identical": stats[3].item() == 0.0, "device_errors": int(stats[4]),
+            "ok": op <= 2e-2 and worst <= 6e-2 and mean <= 2e-3 and tie <= 2e-2 and stats[3].item() == 0.0
             and int(stats[4]) == 0}
