@@ -64,10 +64,20 @@ def copy_cache(src: QwenDecoder, dst: QwenDecoder, tp: int, rank: int) -> None:
     dst.pos.copy_(src.pos)
 
 
+def excess_error(got: torch.Tensor, want: torch.Tensor, ulps: int = 1) -> tuple[float, float]:
+    """(max(|got - want| - ulps x bf16 ulp(want)), RMS(want)): the difference
+    that the outputs' own final roundings (`ulps` of them after the value the
+    two computations sum in different fp32 orders) do not explain."""
+    w = want.float()
+    ulp = torch.ldexp(torch.ones_like(w), torch.frexp(w)[1] - 8)
+    err = float(((got.float() - w).abs() - ulps * ulp).clamp_min(0).max())
+    return err, float(w.pow(2).mean().sqrt())
+
+
 # Model-level bound between two decodes of the same bf16 weights whose only
 # difference is the fp32 summation order (see logits_close).
 DECODE_MAX_TOL = 6e-2
-DECODE_MEAN_TOL = 2e-3
+DECODE_MEAN_TOL = 5e-3
 
 
 def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = DECODE_MAX_TOL,
@@ -88,17 +98,18 @@ def logits_close(got: torch.Tensor, ref: torch.Tensor, tol: float = DECODE_MAX_T
     that differ only in the GEMV kernel (K-major mma.sync vs column-major
     tcgen05) differ by 2.9-4.3% of the logit RMS (max beyond one ulp, over 2.4M
     logits; mean ~0.1%), and a host restatement with fp32 against fp64
-    accumulation at identical rounding points by 1.9%. One ulp of each logit
-    is its own rounding (near 5 x RMS a bf16 ulp is ~2.6% of the RMS); the
-    bound on top of it, 6e-2, is that floor with headroom, and the mean bound
-    2e-3 keeps the typical difference at rounding level."""
+    accumulation at identical rounding points by 1.9% (mean 0.15%). One ulp
+    of each logit is its own rounding (near 5 x RMS a bf16 ulp is ~2.6% of the
+    RMS); the bound on top of it, 6e-2, is that floor with headroom, and the
+    mean bound 5e-3 keeps the typical difference at rounding level.
+    Returns (ok, max beyond one ulp, RMS, mean)."""
     ref32 = ref.float()
     ulp = torch.ldexp(torch.ones_like(ref32), torch.frexp(ref32)[1] - 8)  # bf16 ulp of each reference logit
     diff = (got.float() - ref32).abs()
     err = float((diff - ulp).clamp_min(0).max())
     rms = float(ref32.pow(2).mean().sqrt())
     mean = float(diff.mean())
-    return err <= tol * rms and mean <= mean_tol * rms, err, rms
+    return err <= tol * rms and mean <= mean_tol * rms, err, rms, mean
 
 
 def near_tie(ref_logits: torch.Tensor, ref_tok: torch.Tensor, got_tok: torch.Tensor, rms: float,
@@ -142,11 +153,11 @@ def _nccl_main() -> int:
     for i in range(steps):
         ref.step()
         dec.graph.replay()
-        ok, err, rms = logits_close(dec.buf["logits"], ref.buf["logits"][:, v0:v0 + nv])
+        ok, err, rms, mean = logits_close(dec.buf["logits"], ref.buf["logits"][:, v0:v0 + nv])
         same_tok = bool(torch.equal(dec.tokens, ref.tokens))
         tie_ok, gap = near_tie(ref.buf["logits"], ref.tokens, dec.tokens, rms)
         ok &= tie_ok
-        report["steps"].append({"err": err, "rms": rms, "tokens_equal": same_tok, "tie_gap": gap})
+        report["steps"].append({"err": err, "mean": mean, "rms": rms, "tokens_equal": same_tok, "tie_gap": gap})
         report["ok"] &= ok
         # ranks must agree on the tokens bit for bit
         gathered = [torch.empty_like(dec.tokens) for _ in range(world)]
