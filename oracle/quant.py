@@ -134,13 +134,11 @@ CM_K = 128     # k of a tile
 def repack_cm(packed: np.ndarray) -> np.ndarray:
     """Tiled column-major layout used by the decode engine (a layout of the
     same codes, no reference counterpart): packed [K_pad/2, N] -> uint8
-    [ceil(N/256), K_pad/128, 4, 256, 16]. Tile (b, s) holds columns 256 b ..
-    256 b + 255 and k = 128 s .. 128 s + 127 as 4 chunks of 32 k; chunk c,
-    column r is 16 bytes = 4 little-endian 32-bit words, word w holding
-    k = 128 s + 32 c + 8 w .. + 7 with nibble p = code[8w + 2p] and nibble
-    p + 4 = code[8w + 2p + 1] of that run (p = 0..3). Chunk-major order makes
-    one 16-byte load per column of a warp's 32 consecutive columns read 512
-    contiguous bytes. Columns >= N are zero."""
+    [ceil(N/256), K_pad/128, 256, 64]. Tile (b, s) row r is column 256 b + r,
+    k = 128 s .. 128 s + 127: little-endian 32-bit word w holds k = 8w..8w+7 of
+    the tile with nibble p = code[8w + 2p] and nibble p + 4 = code[8w + 2p + 1]
+    (p = 0..3); 16-byte chunk c of the row is stored at c ^ ((r // 2) % 4).
+    Columns >= N are zero."""
     codes = unpack_int4(packed).astype(np.uint32)  # [K_pad, N]
     kp, n = codes.shape
     if kp % CM_K:
@@ -148,26 +146,36 @@ def repack_cm(packed: np.ndarray) -> np.ndarray:
     nb = -(-n // CM_COLS)
     full = np.zeros((kp, nb * CM_COLS), np.uint32)
     full[:, :n] = codes
-    c = full.T.reshape(nb, CM_COLS, kp // CM_K, 4, 4, 8)  # [block, col, stage, chunk, word, k in word]
-    words = np.zeros(c.shape[:5], np.uint32)
+    c = full.T.reshape(nb, CM_COLS, kp // CM_K, 16, 8)  # [block, row, stage, word, k in word]
+    words = np.zeros(c.shape[:4], np.uint32)
     for p in range(4):
         words |= c[..., 2 * p] << (4 * p)
         words |= c[..., 2 * p + 1] << (4 * p + 16)
-    words = words.transpose(0, 2, 3, 1, 4)  # [block, stage, chunk, col, word]
-    return np.ascontiguousarray(words).astype("<u4").view(np.uint8).reshape(nb, kp // CM_K, 4, CM_COLS, 16)
+    words = words.transpose(0, 2, 1, 3)  # [block, stage, row, word]
+    chunks = words.reshape(nb, kp // CM_K, CM_COLS, 4, 4)  # 16-byte chunks of 4 words
+    out = np.empty_like(chunks)
+    rows = np.arange(CM_COLS)
+    for ch in range(4):
+        out[:, :, rows, ch ^ ((rows // 2) % 4)] = chunks[:, :, rows, ch]
+    return out.astype("<u4").view(np.uint8).reshape(nb, kp // CM_K, CM_COLS, 64)
 
 
 def unpack_cm(tiles: np.ndarray, n: int) -> np.ndarray:
-    """Inverse of ``repack_cm``: tiles [NB, S, 4, 256, 16] -> codes [K_pad, n]."""
+    """Inverse of ``repack_cm``: tiles [NB, S, 256, 64] -> codes [K_pad, n]."""
     t = np.ascontiguousarray(tiles, dtype=np.uint8)
     nb, ns = t.shape[:2]
-    words = t.view("<u4").reshape(nb, ns, 4, CM_COLS, 4).astype(np.uint32)
-    codes = np.empty((nb, ns, 4, CM_COLS, 4, 8), np.uint8)
+    chunks = t.view("<u4").reshape(nb, ns, CM_COLS, 4, 4).astype(np.uint32)
+    rows = np.arange(CM_COLS)
+    logical = np.empty_like(chunks)
+    for ch in range(4):
+        logical[:, :, rows, ch] = chunks[:, :, rows, ch ^ ((rows // 2) % 4)]
+    words = logical.reshape(nb, ns, CM_COLS, 16)
+    codes = np.empty((nb, ns, CM_COLS, 16, 8), np.uint8)
     for p in range(4):
         codes[..., 2 * p] = (words >> (4 * p)) & 15
         codes[..., 2 * p + 1] = (words >> (4 * p + 16)) & 15
-    # [block, stage, chunk, col, word, k in word] -> [k, column]
-    k_major = codes.transpose(1, 2, 4, 5, 0, 3).reshape(ns * CM_K, nb * CM_COLS)
+    # [block, stage, row, k in stage] -> [k, column]
+    k_major = codes.reshape(nb, ns, CM_COLS, CM_K).transpose(1, 3, 0, 2).reshape(ns * CM_K, nb * CM_COLS)
     return k_major[:, :n].copy()
 
 

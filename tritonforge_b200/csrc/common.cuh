@@ -114,13 +114,34 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 // the device error word) when the phase did not complete within `limit_ns`.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: kernels here run for microseconds
 
+// Spins on try_wait (which itself blocks in hardware for a short time) and
+// reads the clock every 64 tries: waits on the critical path of a pipeline
+// return as soon as the phase completes. (A try_wait with a suspend-time hint
+// can sleep well past the completion of the phase.)
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err_word,
                                                   int err_bits, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) {
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
+      if (err_word) atomicOr(err_word, err_bits);
+      return false;
+    }
+  }
+}
+
+// The same bound for long waits off the critical path (an epilogue waiting
+// for a whole segment of MMAs): a short sleep between tries leaves the issue
+// slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_bounded_relaxed(uint64_t* bar, uint32_t parity, int* err_word,
+                                                          int err_bits, uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(128);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       if (err_word) atomicOr(err_word, err_bits);
       return false;
     }

@@ -342,6 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // every warp converged (lane 0 of the copy and MMA warps ran their loops
+  // alone) before the aligned barriers below
+  __syncwarp();
+
   // ------------------------------------------------------------ epilogue
   // The ring is free once every MMA completed: reuse it as cta[NTOK][kRedPitch].
   float* cta = reinterpret_cast<float*>(smem);

@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bready = full + kStages;                                      // dequantised tile written
   uint64_t* freed = bready + kStages;                                     // MMAs of the slot done
   uint64_t* accum = freed + kStages;                                      // all MMAs done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* alldone = accum + 1;                                          // every warp finished its role
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(alldone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&freed[i], 1);
     }
     mbar_init(accum, 1);
+    mbar_init(alldone, kThreads / 32);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&freed[slot]);
       }
       umma_commit(accum);  // arrives once every MMA issued above has completed
+      mbar_wait_bounded(accum, 0u, args.err, 8);  // this warp reports done only after them
     }
   } else {
     // ------------------------------------------------------ dequantisation
@@ -295,9 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  // Teardown: the TMA and MMA warps diverge (one lane works), and an aligned
+  // CTA barrier reached by part of a warp may count the whole warp, so each
+  // warp converges and reports on an mbarrier that warp 0 waits for (bounded)
+  // before freeing the tensor memory.
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if (lane == 0) mbar_arrive(alldone);
   if (warp == 0) {
+    mbar_wait_bounded(alldone, 0u, args.err, 64);
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
   }

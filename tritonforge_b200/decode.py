@@ -449,7 +449,9 @@ class QwenDecoder:
         cm = isinstance(ql, CMLinear)
         kp = ql.scales.shape[0] * ql.group_size
         n = ql.scales.shape[1]
-        ws = _lib.workspaces.get(self.dev, 256)
+        need = (self._lib.tf_qlinear_cm_workspace_bytes(m, n, kp) if cm
+                else self._lib.tf_qlinear_workspace_bytes(m, n, kp, ql.group_size))
+        ws = _lib.workspaces.get(self.dev, need)
         fn = self._lib.tf_qlinear_cm_partial if cm else self._lib.tf_qlinear_partial
         _lib.check(fn(x.data_ptr(), x.stride(0), self._dt, (ql.tiles if cm else ql.packed).data_ptr(),
                       ql.scales.data_ptr(), ql.zeros.data_ptr(), _lib.dtype_code(ql.scales.dtype), out.data_ptr(),
@@ -660,6 +662,15 @@ def _layer_kv(cache, li: int):
     return cache[li][0], cache[li][1]
 
 
+# Bounds on the logits of two decodes of the same bf16 weights whose only
+# difference is the fp32 summation order (max beyond one ulp of each logit, and
+# mean, over the logit RMS): the measured noise floor of that effect without any
+# tensor parallelism (two single-GPU decodes through different GEMV kernels)
+# reaches 4.7% max and 0.58% mean; these are that floor with headroom.
+DECODE_MAX_TOL = 6e-2
+DECODE_MEAN_TOL = 1e-2
+
+
 @torch.no_grad()
 def _row_parallel_op_error(name: str, ref: "QwenDecoder", dec: "QwenDecoder", world: int, rank: int,
                            seed: int) -> float:
@@ -768,8 +779,9 @@ def tp_parity(name: str, group, batch: int, layers: int = 2, steps: int = 4, see
             # whole decodes: logits after `layers` layers, beyond one bf16 ulp of each logit, and the
             # mean; bounded by the summation-order noise floor of a bf16 decode
             "logits_max_err_over_rms": worst, "logits_max_abs_err_over_rms": float(stats[5]),
-            "logits_mean_err_over_rms": mean, "logits_tolerance": {"max": 6e-2, "mean": 2e-3},
+            "logits_mean_err_over_rms": mean, "logits_tolerance": {"max": DECODE_MAX_TOL, "mean": DECODE_MEAN_TOL},
             "tokens_equal": stats[1].item() == 0.0, "near_tie_gap_over_rms": tie,
             "ranks_identical": stats[3].item() == 0.0, "device_errors": int(stats[4]),
-            "ok": op <= 2e-2 and worst <= 6e-2 and mean <= 2e-3 and tie <= 2e-2 and stats[3].item() == 0.0
+            "ok": op <= 2e-2 and worst <= DECODE_MAX_TOL and mean <= DECODE_MEAN_TOL and tie <= 2e-2
+            and stats[3].item() == 0.0
             and int(stats[4]) == 0}
