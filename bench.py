@@ -456,6 +456,16 @@ def run_ours(args) -> None:
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
     e2e_value = seqs * args.steps / (e2e_ms / 1000.0)
 
+    # ---- where the step's time goes: each part of the step replayed alone
+    # (GEMV launches, attention, reductions + norms, embedding/lm_head/argmax),
+    # device-timed, max over ranks; "other" is the step minus their sum (below
+    # zero when the parts overlap in the full step: each kernel's prologue runs
+    # under the previous one's tail through programmatic dependent launch)
+    parts = dec.time_parts()
+    breakdown = {k: _max_over_ranks(v, world) for k, v in parts.items()}
+    breakdown["step"] = ms / args.steps
+    breakdown["other"] = breakdown["step"] - sum(breakdown[k] for k in parts)
+
     peaks = _peaks()
     roof = gemv_roofline(dec, peaks["hbm_gbs"])
     roof["peak_source"] = peaks["source"]
@@ -500,6 +510,7 @@ def run_ours(args) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roof,
             "cpu_baseline": cpu,
+            "step_breakdown_ms": breakdown,
         }
         if parity is not None:
             line["tp_parity"] = parity

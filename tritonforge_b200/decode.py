@@ -459,18 +459,27 @@ class QwenDecoder:
                       _lib.stream_ptr(self.dev)), "qlinear_partial")
 
     def _row_parallel(self, x: torch.Tensor, ql, which: str, res: torch.Tensor, weight: torch.Tensor,
-                      normed: torch.Tensor, summed: torch.Tensor) -> None:
+                      normed: torch.Tensor, summed: torch.Tensor, parts=None) -> None:
         """o_proj / down_proj followed by the residual add and the next RMSNorm.
         Single GPU: the projection rounds its own output. Tensor parallel: an
         fp32 partial per rank, summed across ranks in fp32 (the fused peer-memory
-        kernel, or an NCCL all-reduce), rounded once, then residual + RMSNorm."""
+        kernel, or an NCCL all-reduce), rounded once, then residual + RMSNorm.
+        `parts` (a set of step parts, None for all) selects the projection
+        ("gemv") and the reduction + norm ("reduce")."""
         b = self.buf
+        gemv = parts is None or "gemv" in parts
+        reduce = parts is None or "reduce" in parts
         if not self.tp:
-            self._lin(x, ql, b[which])
-            kernels.rmsnorm_residual(b[which], res, weight, self.eps, out=(normed, summed))
+            if gemv:
+                self._lin(x, ql, b[which])
+            if reduce:
+                kernels.rmsnorm_residual(b[which], res, weight, self.eps, out=(normed, summed))
             return
         part = b[which + "_part"]
-        self._lin_partial(x, ql, part)
+        if gemv:
+            self._lin_partial(x, ql, part)
+        if not reduce:
+            return
         if self.fused_allreduce:
             self._ar_norm(which, res, weight, normed, summed)
             return
@@ -488,40 +497,88 @@ class QwenDecoder:
 
         dist.all_reduce(t, group=self.group)
 
+    STEP_PARTS = ("gemv", "attention", "reduce", "head")
+
     @torch.no_grad()
     def step(self) -> torch.Tensor:
         """One decode step: consumes self.tokens at self.pos, writes the next
         tokens into self.tokens and advances self.pos (all on device)."""
+        return self._step(None)
+
+    def _step(self, parts) -> torch.Tensor:
+        """The step's launches, or only those of the given parts (a subset of
+        STEP_PARTS: the int4 projections; RoPE + KV append + attention; the
+        row-parallel reductions, residual adds and norms; embedding, lm_head and
+        argmax), in the step's order on the same buffers, for timing each part
+        on its own."""
+        def on(p: str) -> bool:
+            return parts is None or p in parts
+
         b = self.buf
         lib, st = self._lib, _lib.stream_ptr(self.dev)
-        torch.index_select(self.embed, 0, self.tokens, out=b["x"])
+        if on("head"):
+            torch.index_select(self.embed, 0, self.tokens, out=b["x"])
         res, res_next = b["res_a"], b["res_b"]
         posp = self.pos.data_ptr()
-        lenp = posp + 4
         nl = len(self.layers)
         for li, L in enumerate(self.layers):
-            if li == 0:
+            if li == 0 and on("head"):
                 kernels.rmsnorm(b["x"], L["in_norm"], self.eps, out=b["normed"])
                 res.copy_(b["x"])
-            self._lin(b["normed"], L["qkv"], b["qkv"])
-            _lib.check(lib.tf_decode_attention_rope(
-                b["qkv"].data_ptr(), b["qkv"].stride(0), self.cos.data_ptr(), self.sin.data_ptr(),
-                self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), posp, b["attn"].data_ptr(), self.B,
-                self.Hq, self.Hkv, self.D, self.T, self.scale, self._dt, st), "decode_attention_rope")
-            self._row_parallel(b["attn"], L["o"], "o", res, L["post_norm"], b["normed"], res_next)
+            if on("gemv"):
+                self._lin(b["normed"], L["qkv"], b["qkv"])
+            if on("attention"):
+                _lib.check(lib.tf_decode_attention_rope(
+                    b["qkv"].data_ptr(), b["qkv"].stride(0), self.cos.data_ptr(), self.sin.data_ptr(),
+                    self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), posp, b["attn"].data_ptr(), self.B,
+                    self.Hq, self.Hkv, self.D, self.T, self.scale, self._dt, st), "decode_attention_rope")
+            self._row_parallel(b["attn"], L["o"], "o", res, L["post_norm"], b["normed"], res_next, parts)
             res, res_next = res_next, res
-            self._gate_up(b["normed"], L["gu"], b["act"])
+            if on("gemv"):
+                self._gate_up(b["normed"], L["gu"], b["act"])
             # the next layer's input norm, or the final norm after the last layer
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < nl else self.final_norm
-            self._row_parallel(b["act"], L["down"], "mlp", res, nxt, b["normed"], res_next)
+            self._row_parallel(b["act"], L["down"], "mlp", res, nxt, b["normed"], res_next, parts)
             res, res_next = res_next, res
-        torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
-        if self.vocab_parallel:
-            self._vocab_parallel_argmax()
-        else:
-            torch.argmax(b["logits"], dim=-1, out=self.tokens)
-        self.pos.add_(1)
+        if on("head"):
+            torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
+            if self.vocab_parallel:
+                self._vocab_parallel_argmax()
+            else:
+                torch.argmax(b["logits"], dim=-1, out=self.tokens)
+            self.pos.add_(1)
         return self.tokens
+
+    @torch.no_grad()
+    def time_parts(self, reps: int = 10) -> dict:
+        """Device time (ms) of each step part replayed alone in a CUDA graph of
+        its own (every rank runs the same parts in the same order, so the
+        reductions' collectives match); tokens and position are restored."""
+        out = {}
+        saved = (self.tokens.clone(), self.pos.clone())
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        for name in self.STEP_PARTS:
+            with torch.cuda.stream(s):
+                self._step({name})  # outside capture: workspaces and kernel attributes
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._step({name})
+            g.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                e0.record(s)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(s)
+            torch.cuda.synchronize(self.dev)
+            out[name] = e0.elapsed_time(e1) / reps
+            del g  # a graph holding collectives goes before the process group does
+        self.tokens.copy_(saved[0])
+        self.pos.copy_(saved[1])
+        torch.cuda.synchronize(self.dev)
+        return out
 
     def _vocab_parallel_argmax(self) -> None:
         """Greedy token over the whole vocabulary from each rank's slice of the
