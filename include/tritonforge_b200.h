@@ -295,6 +295,41 @@ int tf_allreduce_rmsnorm_residual(const uint64_t* peer_buffers, const uint64_t* 
                                   void* normed, void* summed, int64_t M, int64_t N, float eps, int dtype,
                                   int partial_dtype, int* error_word, void* stream);
 
+/* The decode step's head (no reference counterpart: the reference patches only
+ * the decoder layers, integration/qwen.py:155-185, and leaves the embedding
+ * lookup, the lm_head matmul and the greedy argmax to transformers).
+ *
+ * tf_embed_gather: x[b, :] = embed[tokens[b], :] for b < B, and the same rows
+ * into `res` when it is not null (the residual stream starts as the
+ * embedding). tokens are int64; a token outside [0, V) gives a zero row. Rows
+ * are whole 16-byte chunks, pointers 16-byte aligned; dtype TF_F16, TF_BF16
+ * or TF_F32. */
+int tf_embed_gather(const void* embed, int64_t lde, const int64_t* tokens, void* x, int64_t ldx, void* res,
+                    int64_t ldr, int64_t V, int64_t H, int64_t B, int32_t dtype, void* stream);
+
+/* tf_lm_head_argmax: logits[b, v] = round(sum_k x[b, k] * w[v, k]) for a
+ * [V, H] weight (ldw elements per row), B <= 64 rows of x, fp32 accumulation
+ * and one rounding to `dtype` (TF_F16 or TF_BF16), and the greedy argmax over
+ * the rounded logits with ties to the smallest id (torch.argmax's first
+ * maximum). Outputs, each optional (at least one given): `logits` [B, ldl];
+ * `tokens` [B] int64 ids; `best` [B, 2] fp32 (best logit, global id) for a
+ * vocabulary slice whose ids start at v0 (vocabulary-parallel tensor
+ * parallelism, then tf_best_of_ranks); ids are reported as id + v0. `pos`
+ * (n_pos int32 counters, may be null) is advanced by one once the tokens are
+ * written. H % 128 == 0; ldx, ldw multiples of 8; x, w 16-byte aligned.
+ * `workspace` holds tf_lm_head_workspace_bytes(B) zeroed bytes (the error
+ * word, as tf_qlinear, then a counter the kernel leaves zeroed and per-CTA
+ * partial results). */
+size_t tf_lm_head_workspace_bytes(int64_t B);
+int tf_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t V, int64_t H, int64_t B,
+                      int32_t dtype, void* logits, int64_t ldl, int64_t* tokens, float* best, int64_t v0,
+                      int32_t* pos, int32_t n_pos, void* workspace, size_t workspace_bytes, void* stream);
+
+/* tf_best_of_ranks: greedy ids [B] (int64) from every rank's (best logit,
+ * global id) pairs [world][B][2] (fp32), ranks holding consecutive vocabulary
+ * slices in rank order: the largest logit wins, ties to the lowest rank. */
+int tf_best_of_ranks(const float* all_best, int64_t* tokens, int32_t world, int64_t B, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

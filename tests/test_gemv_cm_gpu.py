@@ -116,7 +116,7 @@ def test_decoder_colmajor_matches_kmajor(batch):
     b = QwenDecoder(w, batch, 96)  # batch 9..64: column-major by default
     assert isinstance(a.layers[0]["qkv"], QuantLinear) and isinstance(w.layers[0]["gu"], QuantLinear)
     assert all(isinstance(b.layers[0][n], CMLinear) for n in ("qkv", "o", "gu", "down"))
-    assert b.launches_per_step() == 7 * 2 + 1
+    assert b.launches_per_step() == 7 * 2 + 3  # + embedding gather, first norm, lm_head + argmax
     for d in (a, b):
         d.fill_cache(40, seed=2)
     for _ in range(3):

@@ -72,6 +72,11 @@ SIGNATURES = {
                                   _vp, _sz, _vp]),
     "tf_qlinear_cm_partial": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                      _vp, _sz, _vp]),
+    "tf_embed_gather": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "tf_lm_head_workspace_bytes": (_sz, [_i64]),
+    "tf_lm_head_argmax": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _i32,
+                                 _vp, _sz, _vp]),
+    "tf_best_of_ranks": (_i32, [_vp, _vp, _i32, _i64, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -143,10 +148,12 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 class _Workspaces:
     """Zero-initialised scratch handed to the kernels, one buffer per (device,
-    stream). The kernels use only its 256-byte header: word 0 is the device
+    stream). Its 256-byte header is shared by every kernel: word 0 is the device
     error word of their bounded waits (a wait that gives up after 1 s sets a
-    bit there and the launch still reports success). Calls that share a buffer
-    are ordered on their stream. ``errors`` reads the word of every buffer.
+    bit there and the launch still reports success). After the header only
+    tf_lm_head_argmax keeps anything: a counter it leaves zeroed and per-CTA
+    partial results. Calls that share a buffer are ordered on their stream.
+    ``errors`` reads the word of every buffer.
 
     A buffer is zeroed only when it is (re)allocated. Reallocation happens
     outside any CUDA-graph capture: callers that capture size it first with

@@ -14,8 +14,9 @@ docs/FINAL_REPORT.md:93-99). Per layer:
     qlinear_swiglu(normed, [gate|up])          -> act = silu(gate) * up (one GEMV, fused epilogue)
     quantized_linear(act, down)                -> mlp_out
 
-then rmsnorm_residual(mlp_out, residual, final_norm), the tied fp16 lm_head
-(cuBLAS) and argmax. The math of each step is the reference patched model's
+then rmsnorm_residual(mlp_out, residual, final_norm), and the lm_head GEMV with
+the greedy argmax fused (tf_lm_head_argmax); a step starts with the embedding
+gather (tf_embed_gather). The math of each step is the reference patched model's
 (reference src/tritonforge/integration/qwen.py:101-152): the end-of-layer
 `residual + hidden` of the reference is the `summed` output of the next
 rmsnorm_residual (same rounding). q|k|v are the reference's separate
@@ -382,7 +383,6 @@ class QwenDecoder:
         if self.vocab_parallel:
             self.buf["best"] = torch.empty(B, 2, dtype=torch.float32, device=dev)     # (logit, token id)
             self.buf["all_best"] = torch.empty(self.world, B, 2, dtype=torch.float32, device=dev)
-            self.buf["arg"] = torch.empty(B, dtype=torch.long, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self._lib = _lib.load()
         self._dt = _lib.dtype_code(dt)
@@ -516,15 +516,18 @@ class QwenDecoder:
 
         b = self.buf
         lib, st = self._lib, _lib.stream_ptr(self.dev)
-        if on("head"):
-            torch.index_select(self.embed, 0, self.tokens, out=b["x"])
         res, res_next = b["res_a"], b["res_b"]
+        if on("head"):
+            # x = res = embed[tokens] (the residual stream starts as the embedding)
+            _lib.check(lib.tf_embed_gather(self.embed.data_ptr(), self.embed.stride(0), self.tokens.data_ptr(),
+                                           b["x"].data_ptr(), b["x"].stride(0), res.data_ptr(), res.stride(0),
+                                           self.embed.shape[0], self.embed.shape[1], self.B,
+                                           _lib.dtype_code(self.embed.dtype), st), "embed_gather")
         posp = self.pos.data_ptr()
         nl = len(self.layers)
         for li, L in enumerate(self.layers):
             if li == 0 and on("head"):
                 kernels.rmsnorm(b["x"], L["in_norm"], self.eps, out=b["normed"])
-                res.copy_(b["x"])
             if on("gemv"):
                 self._lin(b["normed"], L["qkv"], b["qkv"])
             if on("attention"):
@@ -541,12 +544,17 @@ class QwenDecoder:
             self._row_parallel(b["act"], L["down"], "mlp", res, nxt, b["normed"], res_next, parts)
             res, res_next = res_next, res
         if on("head"):
-            torch.matmul(b["normed"], self.lm_head.t(), out=b["logits"])
-            if self.vocab_parallel:
+            # logits, the greedy token (or this rank's best (logit, id) pairs) and pos += 1 in one kernel
+            vp = self.vocab_parallel
+            ws = _lib.workspaces.get(self.dev, self._lib.tf_lm_head_workspace_bytes(self.B))
+            _lib.check(lib.tf_lm_head_argmax(
+                b["normed"].data_ptr(), b["normed"].stride(0), self.lm_head.data_ptr(), self.lm_head.stride(0),
+                self.lm_head.shape[0], self.lm_head.shape[1], self.B, _lib.dtype_code(self.lm_head.dtype),
+                b["logits"].data_ptr(), b["logits"].stride(0), None if vp else self.tokens.data_ptr(),
+                b["best"].data_ptr() if vp else None, self.v0 if vp else 0, self.pos.data_ptr(), self.pos.numel(),
+                ws.data_ptr(), ws.numel(), st), "lm_head_argmax")
+            if vp:
                 self._vocab_parallel_argmax()
-            else:
-                torch.argmax(b["logits"], dim=-1, out=self.tokens)
-            self.pos.add_(1)
         return self.tokens
 
     @torch.no_grad()
@@ -583,17 +591,14 @@ class QwenDecoder:
     def _vocab_parallel_argmax(self) -> None:
         """Greedy token over the whole vocabulary from each rank's slice of the
         logits. Ties go to the smallest token id, as torch.argmax over the full
-        logits does (the first maximum): within a rank argmax takes the first,
-        across ranks the lowest rank (whose ids are smaller) wins."""
+        logits does (the first maximum): within a rank the lm_head kernel keeps
+        the first, across ranks the lowest rank (whose ids are smaller) wins."""
         import torch.distributed as dist
 
-        from .tp import best_of_ranks, local_best
-
         b = self.buf
-        local_best(b["logits"], self.v0, b["best"], b["arg"])
         dist.all_gather_into_tensor(b["all_best"].view(-1, 2), b["best"], group=self.group)
-        tok = best_of_ranks(b["all_best"])
-        self.tokens.copy_(tok)
+        _lib.check(self._lib.tf_best_of_ranks(b["all_best"].data_ptr(), self.tokens.data_ptr(), self.world, self.B,
+                                              _lib.stream_ptr(self.dev)), "best_of_ranks")
 
     def _gate_up(self, x: torch.Tensor, ql, act: torch.Tensor) -> None:
         """act = silu(x @ Wg) * (x @ Wu): one fused decode kernel for up to 32
@@ -615,8 +620,10 @@ class QwenDecoder:
         kernels.swiglu(gu[:, :, 0], gu[:, :, 1], out=act.view(m, -1, 64))
 
     def launches_per_step(self) -> int:
-        """Kernels of this library launched by one step."""
-        n = 1
+        """Kernels of this library launched by one step: the embedding gather,
+        the first RMSNorm, 7 or 8 per layer, the lm_head + argmax and, under
+        vocabulary-parallel tensor parallelism, best_of_ranks."""
+        n = 3 + (1 if self.vocab_parallel else 0)
         for L in self.layers:
             fused = self.B <= (64 if isinstance(L["gu"], CMLinear) else 32)
             n += 7 if fused else 8
