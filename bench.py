@@ -303,23 +303,28 @@ def _config(args) -> dict:
             "l2": "per-step working set (int4 weights + lm_head) exceeds the 126 MB L2"}
 
 
-def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
+def gemv_roofline(dec, peak_gbs: float, reps: int = 20, batch_rows: int | None = None) -> dict:
     """Time the step's int4 GEMV launches alone (same shapes, weights and
-    inputs) in a CUDA graph; achieved = algorithmic bytes / measured time."""
+    inputs) in a CUDA graph; achieved = algorithmic bytes / measured time.
+    With `batch_rows`, the same launches on the first rows of the step's
+    buffers (the same weights at a smaller batch, 1 for batch-1 decode)."""
     import torch
 
     from tritonforge_b200 import kernels
 
     b = dec.buf
-    launches = []
+    rows = slice(0, batch_rows) if batch_rows else slice(None)
+    launches = []  # (x, weights, out, fused gate|up + SwiGLU)
     for L in dec.layers:
-        launches += [(b["normed"], L["qkv"], b["qkv"]), (b["attn"], L["o"], b["o"]),
-                     (b["normed"], L["gu"], b["act"]), (b["act"], L["down"], b["mlp"])]
+        launches += [(b["normed"][rows], L["qkv"], b["qkv"][rows], False),
+                     (b["attn"][rows], L["o"], b["o"][rows], False),
+                     (b["normed"][rows], L["gu"], b["act"][rows], True),
+                     (b["act"][rows], L["down"], b["mlp"][rows], False)]
 
     def run():
-        for x, ql, out in launches:
-            if out is b["act"]:
-                dec._gate_up(x, ql, out)  # fused gate|up + SwiGLU (the step's own launch)
+        for x, ql, out, gate_up in launches:
+            if gate_up:
+                dec._gate_up(x, ql, out)  # the step's own fused launch
             else:
                 dec._lin(x, ql, out)
 
@@ -343,7 +348,7 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20) -> dict:
     total_us = e0.elapsed_time(e1) * 1e3 / reps
     alg = 0
     kinds = set()
-    for x, ql, out in launches:
+    for x, ql, out, _ in launches:
         m, k = x.shape
         kp, n = ql.scales.shape[0] * ql.group_size, ql.scales.shape[1]
         kinds.add(type(ql).__name__)
@@ -469,6 +474,7 @@ def run_ours(args) -> None:
     peaks = _peaks()
     roof = gemv_roofline(dec, peaks["hbm_gbs"])
     roof["peak_source"] = peaks["source"]
+    roof_m1 = gemv_roofline(dec, peaks["hbm_gbs"], batch_rows=1) if args.batch > 1 else None
     # DRAM traffic: an ncu capture of one GEMV launch (read + write bytes over
     # its algorithmic bytes, committed under profiles/), scaled to the step
     traffic_file = {"gemv_int4 (mma.sync, K-major weights)": "gemv_dram_traffic.json",
@@ -512,6 +518,9 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "step_breakdown_ms": breakdown,
         }
+        if roof_m1 is not None:
+            # the same step's projections at M = 1 (one decode row, the same weights and layout)
+            line["roofline_m1"] = roof_m1
         if parity is not None:
             line["tp_parity"] = parity
         print(json.dumps(line), flush=True)
