@@ -4,21 +4,23 @@
 // Replaces the reference's large-M path, which either re-dequantises the
 // weight tile for every row tile (src/tritonforge/kernels/dequant_gemm.py:39-113)
 // or dequantises the whole weight and calls cuBLAS (integration/qwen.py:91-97).
-// Here each CTA owns 128 output columns and a group of up to 512 rows
-// (4 row tiles of 128) and walks K in chunks of 64:
+// Here each CTA owns 256 output columns and a group of up to 256 rows
+// (2 row tiles of 128) and walks K in chunks of 64 through a 3-stage ring:
 //  * a TMA warp loads, per chunk, the x tiles of the row tiles ([128 rows x
 //    64 k], 128-byte swizzle: the K-major UMMA canonical layout), the packed
-//    weights [32 packed rows x 128 columns] and the chunk's scale/zero rows;
-//  * 4 dequantisation warps turn the packed chunk into a [64 k x 128 n] tile
+//    weights [32 packed rows x 256 columns] and the chunk's scale/zero rows;
+//  * 4 dequantisation warps turn the packed chunk into a [64 k x 256 n] tile
 //    of the activation type in shared memory, once for all row tiles, in the
 //    MN-major 128-byte-swizzled UMMA layout, with the reference's rounding:
 //    w = round_x((code - zero) * scale) (quant.py:90-105, reference.py:21-35).
 //    A nibble becomes (O + code) with one lop3 against a magic exponent, the
 //    subtraction of (O + zero) is exact and the multiply by the scale rounds
 //    once, so every weight equals the oracle's bit for bit;
-//  * one thread issues tcgen05.mma (kind::f16, M=128, N=128, K=16, fp32
-//    accumulators in TMEM: 4 row tiles x 128 columns = all 512 columns) and
-//    commits each chunk to an mbarrier that frees its ring slot;
+//  * one thread issues tcgen05.mma (kind::f16, M=128, N=256, K=16: the shape
+//    that runs at the tensor pipe's full rate; fp32 accumulators in TMEM, 2 row
+//    tiles x 256 columns = all 512 columns) and commits each chunk to an
+//    mbarrier that frees its ring slot. 256 columns per CTA also halve the
+//    re-reads of x against 128-column tiles;
 //  * the 4 dequantisation warps then read the accumulators back with
 //    tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = rows), round to the
 //    activation type, add the bias and round again (reference.py:33-35).
@@ -32,21 +34,21 @@
 namespace tf {
 namespace tc {
 
-constexpr int kN = 128;            // output columns per CTA (UMMA N)
+constexpr int kN = 256;            // output columns per CTA (UMMA N)
 constexpr int kMT = 128;           // rows per row tile (UMMA M)
-constexpr int kMaxTiles = 4;       // row tiles per CTA: 4 x 128 TMEM columns
+constexpr int kMaxTiles = 2;       // row tiles per CTA: 2 x 256 TMEM columns
 constexpr int kKC = 64;            // k per chunk (one 128-byte swizzle atom of halves)
-constexpr int kStages = 2;
+constexpr int kStages = 3;
 constexpr int kDeqWarps = 4;
 constexpr int kThreads = 32 * (kDeqWarps + 2);  // + TMA warp + MMA warp
 
 // stage layout (bytes; the UMMA operand tiles are 1024-byte aligned)
 constexpr int kXTile = kMT * kKC * 2;           // 16 KiB per row tile
 constexpr int kXOff = 0;
-constexpr int kBOff = kMaxTiles * kXTile;       // dequantised [64 k][128 n]: 2 atoms of 64 n x 64 k rows
-constexpr int kBBytes = kKC * kN * 2;           // 16 KiB
-constexpr int kWOff = kBOff + kBBytes;          // packed [32 rows][128 B]
-constexpr int kWBytes = (kKC / 2) * kN;         // 4 KiB
+constexpr int kBOff = kMaxTiles * kXTile;       // dequantised [64 k][256 n]: 4 atoms of 64 n x 64 k rows
+constexpr int kBBytes = kKC * kN * 2;           // 32 KiB
+constexpr int kWOff = kBOff + kBBytes;          // packed [32 rows][256 B]
+constexpr int kWBytes = (kKC / 2) * kN;         // 8 KiB
 constexpr int kSOff = kWOff + kWBytes;
 constexpr int kZOff = kSOff + kN * 2;
 constexpr int kStage = ((kZOff + kN * 2) + 1023) / 1024 * 1024;
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == 0) {
-    // all 512 TMEM columns: 4 row tiles x 128 fp32 accumulator columns
+    // all 512 TMEM columns: 2 row tiles x 256 fp32 accumulator columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -230,10 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const XT* sv = reinterpret_cast<const XT*>(st + kSOff);
       const XT* zv = reinterpret_cast<const XT*>(st + kZOff);
 #pragma unroll
-      for (int item = 0; item < 4; ++item) {
+      for (int item = 0; item < 8; ++item) {
         const int i = tid + 128 * item;
-        const int j = i >> 4;         // packed row: k = 2j, 2j + 1 of the chunk
-        const int cg = i & 15;        // columns 8 cg .. 8 cg + 7
+        const int j = i >> 5;         // packed row: k = 2j, 2j + 1 of the chunk
+        const int cg = i & 31;        // columns 8 cg .. 8 cg + 7
         const uint2 pw = *reinterpret_cast<const uint2*>(st + kWOff + j * kN + 8 * cg);
         const uint4 s4 = *reinterpret_cast<const uint4*>(sv + 8 * cg);
         const uint4 z4 = *reinterpret_cast<const uint4*>(zv + 8 * cg);
@@ -353,7 +355,7 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   int rc = encode_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, (uint64_t)pb.K, (uint64_t)pb.M,
                                 (uint64_t)pb.ldx * 2, kKC, kMT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  // packed weights [K_pad/2 rows, N bytes], box 128 columns x 32 rows
+  // packed weights [K_pad/2 rows, N bytes], box 256 columns x 32 rows
   rc = encode_tensor_map_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, pb.packed, (uint64_t)pb.N,
                             (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, kN, kKC / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
