@@ -618,7 +618,8 @@ def kernel_sweep(args) -> None:
                 flops = 2 * m * n * k
                 rec = {"op": "quantized_linear", "dtype": dname, "M": m, "K": k, "N": n, "us": us,
                        "gbs": alg / us / 1e3, "tflops": flops / us / 1e6,
-                       "regime": "gemv" if m <= 32 else "gemm",
+                       "regime": ("gemv" if m <= 32 else f"gemv x {-(-m // 32)} row chunks" if m <= 128
+                                  else "gemm"),
                        "l2_resident": copies * wbytes < L2}
                 rec["frac_hbm"] = rec["gbs"] / peaks["hbm_gbs"]
                 rec["frac_tensor"] = rec["tflops"] / tflops_peak

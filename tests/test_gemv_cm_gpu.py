@@ -133,7 +133,7 @@ def test_decoder_colmajor_matches_kmajor(batch):
 
 
 @pytest.mark.parametrize("layout,regime,m", [("kmajor", "gemv", 1), ("kmajor", "gemv", 16), ("kmajor", "gemv", 32),
-                                              ("kmajor", "gemm", 64), ("kmajor", "simt", 5), ("cm", "cm", 1),
+                                              ("kmajor", "gemm", 160), ("kmajor", "simt", 5), ("cm", "cm", 1),
                                               ("cm", "cm", 32), ("cm", "cm", 64)])
 def test_qlinear_partial_is_the_unrounded_sum(layout, regime, m):
     """tf_qlinear_partial / tf_qlinear_cm_partial (a row-parallel shard's fp32
@@ -163,7 +163,7 @@ def test_qlinear_partial_is_the_unrounded_sum(layout, regime, m):
                                         ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device))
         else:
             # the partial entry point picks its regime like tf_qlinear; force the others by shape:
-            # simt through an odd stride (ldx not a multiple of 8), gemm through M > 32
+            # simt through an odd stride (ldx not a multiple of 8), gemm through M > 128
             xs = x
             if regime == "simt":
                 xs = torch.zeros(m, k + 1, dtype=dtype, device="cuda")[:, :k]

@@ -264,6 +264,21 @@ def test_gemm_regime(m, n, k, dtype):
     assert torch.equal(out, again), "deterministic"
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", [(33, 512, 896), (64, 3584, 3584), (100, 256, 1024), (128, 896, 4864)])
+def test_auto_regime_between_33_and_128_rows(m, n, k, dtype):
+    """The automatic regime runs 33..128 rows as 32-row chunks of the decode
+    GEMV: every row (the partial last chunk included) against the oracle, and
+    each chunk equal to the decode GEMV on those rows alone."""
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, seed=m + n)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b)
+    ref = oracle_linear(x, packed, scales, zeros, b)
+    assert_rms_close(out, ref, dtype, f"auto {m}x{n}x{k}")
+    for r in range(0, m, 32):
+        alone = kernels.quantized_linear(x[r:r + 32].contiguous(), packed, scales, zeros, b, config={"regime": "gemv"})
+        assert torch.equal(out[r:r + 32], alone)
+
+
 # ---- fused gate|up + SwiGLU (decode regime) --------------------------------
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("m,i,k", [(1, 4864, 896), (8, 4864, 896), (3, 896, 4864), (16, 18944, 3584),
