@@ -27,6 +27,11 @@ restated in oracle/) on this host's cores: for the 0.5B model whole decode
 steps, for 7B/72B one decoder layer plus the lm_head, extrapolated to all
 layers.
 
+For 7B/72B the line also carries `prefill`: the time to first token of one
+2048-token prompt (`--prefill-len`) through the engine's own prefill (the
+tcgen05 int4 GEMM at M = prompt length for every projection), timed before the
+decode weights are converted.
+
 `--impl reference` times that same CPU path as the reference arm (rank 0 only).
 """
 
@@ -55,6 +60,14 @@ def _peaks() -> dict:
         return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
     except Exception:
         return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _peaks_tensor() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return {"bf16_tflops": float(json.load(f)["bf16_tflops"]), "source": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -364,6 +377,65 @@ def gemv_roofline(dec, peak_gbs: float, reps: int = 20, batch_rows: int | None =
             "us_per_launch": total_us / len(launches)}
 
 
+def time_prefill(weights, group, world: int, args, dev) -> dict:
+    """Time to first token of one prompt of `args.prefill_len` random token ids
+    through QwenDecoder.prefill_tokens (batch 1, K-major projections: every
+    projection runs the tcgen05 GEMM at M = prompt length, the library's
+    attention covers the prompt, the lm_head + argmax the last position).
+    Device-timed with the prompt resident, max over ranks; and end to end with
+    the prompt copied from pinned host memory and the first token read back."""
+    import torch
+
+    from tritonforge_b200.decode import QwenDecoder
+
+    n = args.prefill_len
+    pre = QwenDecoder(weights, batch=1, max_len=n + 8, group=group, fused_allreduce=False, colmajor=False)
+    g = torch.Generator().manual_seed(7)
+    host = torch.randint(0, weights.embed.shape[0], (1, n), generator=g).pin_memory()
+    first = torch.empty(1, dtype=torch.long, pin_memory=True)
+    resident = host.to(dev)
+    pre.prefill_tokens(resident)  # warm-up: workspaces, kernel attributes, attention backend
+    torch.cuda.synchronize(dev)
+    reps = max(1, args.prefill_reps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(reps):
+        pre.prefill_tokens(resident)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(reps):
+        first.copy_(pre.prefill_tokens(host), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    errs = pre.device_errors()
+    # projection FLOPs of this rank's shards (2 x rows x K x N per projection)
+    flops = sum(2 * n * L[p].packed.shape[0] * 2 * L[p].packed.shape[1]
+                for L in pre.layers for p in ("qkv", "o", "gu", "down"))
+    pre.release()
+    del pre
+    torch.cuda.empty_cache()
+    if errs:
+        raise RuntimeError(f"prefill kernels reported device error bits {errs}")
+    peak = _peaks_tensor()
+    achieved = flops / (ms / 1000.0) / 1e12
+    return {"prompt_tokens": n, "batch": 1, "reps": reps, "ttft_ms": ms, "tok_per_s": n / (ms / 1000.0),
+            "e2e_ttft_ms": e2e_ms, "h2d_bytes": host.numel() * 8, "d2h_bytes": 8,
+            "projection_tflop_per_gpu": flops / 1e12,
+            "projection_tflops_per_gpu": achieved,
+            "frac_of_bf16_peak": achieved / peak["bf16_tflops"], "peak_source": peak["source"],
+            "note": ("whole prefill time (GEMMs, library attention, RoPE, norms, SwiGLU, lm_head) "
+                     "over the projections' FLOPs alone, against the measured cuBLAS bf16 burst peak")}
+
+
 def run_ours(args) -> None:
     world, rank, local = _dist()
     import torch
@@ -375,7 +447,7 @@ def run_ours(args) -> None:
     torch.cuda.set_device(dev)
     tp = args.model != "0.5b"
     cpu_copy = model = None
-    parity = None
+    parity = prefill = None
     if tp and world > 1 and not args.no_tp_parity:
         # before the timed model is built: the sharded decode of two seeded
         # layers against the same layers decoded on one GPU, on every rank
@@ -395,11 +467,14 @@ def run_ours(args) -> None:
                                             seed=0)
             if cache_dir:
                 weights.save(cache_dir, tp=world, rank=rank)
+        group = dist.group.WORLD if world > 1 else None
+        if args.prefill_len:
+            # before any conversion: the prompt's GEMMs read the K-major layout
+            prefill = time_prefill(weights, group, world, args, dev)
         lo, hi = QwenDecoder.COLMAJOR_BATCH
         if args.layout == "cm" or (args.layout == "auto" and lo <= args.batch <= hi):
             weights.to_colmajor()  # in place: one copy of the weights in HBM
         max_len = args.prompt + args.warmup + 2 * args.steps + 8
-        group = dist.group.WORLD if world > 1 else None
         dec = QwenDecoder(weights, batch=args.batch, max_len=max_len, group=group,
                           fused_allreduce=args.allreduce == "fused", colmajor=args.layout == "cm")
         dec.fill_cache(args.prompt, seed=1)
@@ -523,6 +598,8 @@ def run_ours(args) -> None:
             line["roofline_m1"] = roof_m1
         if parity is not None:
             line["tp_parity"] = parity
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     errs = dec.device_errors()
     if errs:
@@ -741,6 +818,10 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=None, help="context length (default 4096 / 2048 / 128)")
     ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
                     help="tensor parallel: fused all-reduce + RMSNorm over peer memory, or NCCL + RMSNorm")
+    ap.add_argument("--prefill-len", type=int, default=None,
+                    help="prompt tokens of the timed batch-1 prefill (TTFT) of the 7b/72b models; 0 for none "
+                         "(default 2048)")
+    ap.add_argument("--prefill-reps", type=int, default=2, help="timed prefills (after one warm-up)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU decode for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp-parity", action="store_true",
@@ -772,6 +853,8 @@ def main() -> None:
         args.batch = 8 if args.model == "0.5b" else 32
     if args.prompt is None:
         args.prompt = {"72b": 4096, "7b": 2048, "0.5b": 128}[args.model]
+    if args.prefill_len is None:
+        args.prefill_len = 0 if args.model == "0.5b" else 2048
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

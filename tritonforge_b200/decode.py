@@ -544,18 +544,24 @@ class QwenDecoder:
             self._row_parallel(b["act"], L["down"], "mlp", res, nxt, b["normed"], res_next, parts)
             res, res_next = res_next, res
         if on("head"):
-            # logits, the greedy token (or this rank's best (logit, id) pairs) and pos += 1 in one kernel
-            vp = self.vocab_parallel
-            ws = _lib.workspaces.get(self.dev, self._lib.tf_lm_head_workspace_bytes(self.B))
-            _lib.check(lib.tf_lm_head_argmax(
-                b["normed"].data_ptr(), b["normed"].stride(0), self.lm_head.data_ptr(), self.lm_head.stride(0),
-                self.lm_head.shape[0], self.lm_head.shape[1], self.B, _lib.dtype_code(self.lm_head.dtype),
-                b["logits"].data_ptr(), b["logits"].stride(0), None if vp else self.tokens.data_ptr(),
-                b["best"].data_ptr() if vp else None, self.v0 if vp else 0, self.pos.data_ptr(), self.pos.numel(),
-                ws.data_ptr(), ws.numel(), st), "lm_head_argmax")
-            if vp:
-                self._vocab_parallel_argmax()
+            self._head(b["normed"])
         return self.tokens
+
+    def _head(self, x: torch.Tensor) -> None:
+        """Logits of the B rows of x, the greedy tokens into self.tokens (or
+        this rank's best (logit, id) pairs, then the vocabulary-parallel
+        winner) and pos += 1, in one kernel."""
+        b = self.buf
+        vp = self.vocab_parallel
+        ws = _lib.workspaces.get(self.dev, self._lib.tf_lm_head_workspace_bytes(self.B))
+        _lib.check(self._lib.tf_lm_head_argmax(
+            x.data_ptr(), x.stride(0), self.lm_head.data_ptr(), self.lm_head.stride(0),
+            self.lm_head.shape[0], self.lm_head.shape[1], self.B, _lib.dtype_code(self.lm_head.dtype),
+            b["logits"].data_ptr(), b["logits"].stride(0), None if vp else self.tokens.data_ptr(),
+            b["best"].data_ptr() if vp else None, self.v0 if vp else 0, self.pos.data_ptr(), self.pos.numel(),
+            ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)), "lm_head_argmax")
+        if vp:
+            self._vocab_parallel_argmax()
 
     @torch.no_grad()
     def time_parts(self, reps: int = 10) -> dict:
@@ -691,6 +697,89 @@ class QwenDecoder:
             self.v_cache[li, :, :, :t0].copy_(v)
         self.tokens.copy_(out.logits[:, -1, :].argmax(-1))
         self.pos.copy_(torch.tensor([t0, t0 + 1], dtype=torch.int32))
+        return self.tokens.clone()
+
+    @torch.no_grad()
+    def prefill_tokens(self, prompt: torch.Tensor) -> torch.Tensor:
+        """Prefill the prompt [B, T0] through this engine's kernels, one
+        sequence at a time (M = T0 rows per launch): the embedding gather, the
+        norms, every projection through quantized_linear (the tcgen05 GEMM for
+        more than 128 rows; under tensor parallelism the row-parallel fp32
+        partials are all-reduced and rounded once), RoPE with transformers'
+        roundings, causal attention over the prompt (the library's
+        scaled-dot-product attention: the prompt's keys and values are written
+        to the static cache first), and the lm_head + argmax of the last
+        positions. Sets the first generated tokens and the position; needs the
+        reference's K-major projections (QuantLinear; the column-major layout
+        serves up to 64 rows)."""
+        import torch.nn.functional as F
+
+        if prompt.shape[0] != self.B:
+            raise ValueError(f"prompt batch {prompt.shape[0]} != decoder batch {self.B}")
+        t0 = prompt.shape[1]
+        if t0 < 1 or t0 >= self.T:
+            raise ValueError(f"prompt length {t0} does not fit max_len {self.T}")
+        for L in self.layers:
+            if not all(isinstance(L[n], QuantLinear) for n in ("qkv", "o", "gu", "down")):
+                raise RuntimeError("prefill_tokens needs K-major projections (QwenDecoder(..., colmajor=False))")
+        prompt = prompt.to(self.dev, torch.long)
+        dt, dev, H, D = self.embed.dtype, self.dev, self.H, self.D
+        hq, hkv = self.Hq * D, self.Hkv * D
+        lib, st = self._lib, _lib.stream_ptr(self.dev)
+
+        def buf(*shape, dtype=dt):
+            return torch.empty(*shape, dtype=dtype, device=dev)
+
+        x, res_a, res_b, normed = buf(t0, H), buf(t0, H), buf(t0, H), buf(t0, H)
+        qkv, o, gu, act = buf(t0, hq + 2 * hkv), buf(t0, H), buf(t0, 2 * self.I), buf(t0, self.I)
+        part = buf(t0, H, dtype=torch.float32) if self.tp else None
+        last = buf(self.B, H)
+        cos, sin = self.cos[:t0, None, :], self.sin[:t0, None, :]
+
+        def rope(t: torch.Tensor) -> torch.Tensor:
+            # [T0, heads, D]: (t * cos) + (rotate_half(t) * sin), each product and the sum rounded
+            h = D // 2
+            return t * cos + torch.cat((-t[..., h:], t[..., :h]), dim=-1) * sin
+
+        def row_parallel(xin, ql, weight, res, res_next):
+            if self.tp:
+                self._lin_partial(xin, ql, part)
+                self._all_reduce(part)
+                o.copy_(part)  # one rounding of the fp32 sum
+            else:
+                self._lin(xin, ql, o)
+            kernels.rmsnorm_residual(o, res, weight, self.eps, out=(normed, res_next))
+
+        nl = len(self.layers)
+        for b in range(self.B):
+            toks = prompt[b].contiguous()
+            res, res_next = res_a, res_b
+            _lib.check(lib.tf_embed_gather(self.embed.data_ptr(), self.embed.stride(0), toks.data_ptr(), x.data_ptr(),
+                                           H, res.data_ptr(), H, self.embed.shape[0], H, t0,
+                                           _lib.dtype_code(self.embed.dtype), st), "embed_gather")
+            kernels.rmsnorm(x, self.layers[0]["in_norm"], self.eps, out=normed)
+            for li, L in enumerate(self.layers):
+                self._lin(normed, L["qkv"], qkv)
+                q = rope(qkv[:, :hq].view(t0, self.Hq, D))
+                k = rope(qkv[:, hq:hq + hkv].view(t0, self.Hkv, D))
+                v = qkv[:, hq + hkv:].view(t0, self.Hkv, D)
+                self.k_cache[li, b, :, :t0].copy_(k.transpose(0, 1))
+                self.v_cache[li, b, :, :t0].copy_(v.transpose(0, 1))
+                a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], self.k_cache[li, b:b + 1, :, :t0],
+                                                   self.v_cache[li, b:b + 1, :, :t0], is_causal=True,
+                                                   scale=self.scale, enable_gqa=True)
+                attn = a[0].transpose(0, 1).reshape(t0, hq)
+                row_parallel(attn, L["o"], L["post_norm"], res, res_next)
+                res, res_next = res_next, res
+                self._lin(normed, L["gu"], gu)
+                g4 = gu.view(t0, -1, 2, 64)
+                kernels.swiglu(g4[:, :, 0], g4[:, :, 1], out=act.view(t0, -1, 64))
+                nxt = self.layers[li + 1]["in_norm"] if li + 1 < nl else self.final_norm
+                row_parallel(act, L["down"], nxt, res, res_next)
+                res, res_next = res_next, res
+            last[b].copy_(normed[t0 - 1])
+        self.pos.copy_(torch.tensor([t0 - 1, t0], dtype=torch.int32))  # the head advances it to [t0, t0 + 1]
+        self._head(last)
         return self.tokens.clone()
 
     @torch.no_grad()
