@@ -52,6 +52,7 @@ constexpr int kWBytes = (kKC / 2) * kN;         // 8 KiB
 constexpr int kSOff = kWOff + kWBytes;
 constexpr int kZOff = kSOff + kN * 2;
 constexpr int kStage = ((kZOff + kN * 2) + 1023) / 1024 * 1024;
+static_assert(kStages * kStage >= kDeqWarps * 32768, "the epilogue stages 32 KiB per warp in the ring");
 
 struct Args {
   const void* bias;
@@ -116,7 +117,7 @@ template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                         const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
-                        const Args args) {
+                        const __grid_constant__ CUtensorMap omap, const Args args) {
   using D = Deq<XT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -262,42 +263,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    // Once every MMA has completed, the ring is idle (every copy landed and
+    // was consumed): warp w stages its 32 rows of each row tile there, 32 KiB
+    // per warp, as boxes of [32 rows x 128 bytes] in the 128-byte swizzle
+    // (16-byte chunk c of row r at chunk c ^ (r % 8): conflict-free for
+    // row-per-lane writes), and one lane stores the boxes with TMA (rows and
+    // columns outside the output are not written).
     if (mbar_wait_bounded(accum, 0u, args.err, 8)) {
       tc_fence_after();
       pdl_wait();  // output writes follow the previous kernel
-      const int rw = 32 * warp + lane;  // row within a row tile = TMEM lane
+      uint8_t* stage = smem + warp * 32768;
+      const int box_cols = args.out_f32 ? 32 : 64;  // columns per 128-byte box row
+      const uint32_t rsw = (uint32_t)(lane & 7);
       for (int t = 0; t < tiles; ++t) {
-        const int m = m0 + t * kMT + rw;
+        if (t > 0) {  // the previous tile's stores have read the staging area
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
         for (int cc = 0; cc < kN; cc += 32) {
           uint32_t r[32];
           tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + t * kN + cc, r);
-          if (m < args.M && args.out_f32) {
-            float* dst = static_cast<float*>(args.out) + (int64_t)m * args.ldo + n0 + cc;
+          if (args.out_f32) {
+            uint8_t* row = stage + (cc / 32) * 4096 + lane * 128;
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (n0 + cc + e < args.N) dst[e] = __uint_as_float(r[e]);
-          } else if (m < args.M) {
-            XT* dst = static_cast<XT*>(args.out) + (int64_t)m * args.ldo + n0 + cc;
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(row + (((uint32_t)q ^ rsw) << 4)) =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          } else {
+            uint32_t h[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const int col = n0 + cc + e;
-              if (col + 1 < args.N) {
-                float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
-                if (args.bias) {
-                  v0 += load_as_f32(args.bias, col, args.bias_dtype);
-                  v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
-                }
-                dst[e] = Num<XT>::from_f(v0);
-                dst[e + 1] = Num<XT>::from_f(v1);
-              } else if (col < args.N) {
-                float v0 = round_to<XT>(__uint_as_float(r[e]));
-                if (args.bias) v0 += load_as_f32(args.bias, col, args.bias_dtype);
-                dst[e] = Num<XT>::from_f(v0);
+              float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
+              if (args.bias) {
+                const int col = n0 + cc + e;
+                if (col < args.N) v0 += load_as_f32(args.bias, col, args.bias_dtype);
+                if (col + 1 < args.N) v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
               }
+              const XT a = Num<XT>::from_f(v0), b = Num<XT>::from_f(v1);
+              h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
+                         ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
             }
+            uint8_t* row = stage + (cc / 64) * 4096 + lane * 128;
+            const int c0 = (cc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(row + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
+                  make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
           }
         }
+        // the generic-proxy writes become visible to the TMA unit, then one lane stores
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          const int row0 = m0 + t * kMT + 32 * warp;
+          for (int b = 0; b < kN / box_cols; ++b) tma_store_2d(&omap, stage + b * 4096, n0 + b * box_cols, row0);
+          bulk_commit_group();
+        }
       }
+      if (lane == 0) bulk_wait_all();  // the output is written before this CTA reports done
+      __syncwarp();
     }
   }
   // Teardown: the TMA and MMA warps diverge (one lane works), and an aligned
@@ -323,6 +347,8 @@ bool gemm_supported(const QLinearProblem& pb) {
   if (pb.N % 16 != 0 || pb.ldx % 8 != 0) return false;
   if (!aligned(pb.x, 16) || !aligned(pb.packed, 16) || !aligned(pb.scales, 16) || !aligned(pb.zeros, 16))
     return false;
+  // the output is stored with TMA: 16-byte aligned base and row pitch
+  if (!aligned(pb.out, 16) || (pb.ldo * (pb.out_f32 ? 4 : 2)) % 16 != 0) return false;
   if (pb.M > 0x7fffffffLL || pb.N > 0x7fffffffLL) return false;
   return true;
 }
@@ -342,7 +368,7 @@ static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cu
     attr_set[dev] = true;
   }
   return launch_ex("gemm_int4_tc", kern, grid, dim3(kThreads), smem, st, dim3(1, 1, 1), maps[0], maps[1], maps[2],
-                   maps[3], a);
+                   maps[3], maps[4], a);
 }
 
 int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
@@ -350,7 +376,7 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   if (!pb.workspace || pb.workspace_bytes < kWsHeader)
     return fail(TF_ERR_WORKSPACE, "qlinear(gemm): workspace %zu bytes < required %zu", pb.workspace_bytes,
                 (size_t)kWsHeader);
-  CUtensorMap maps[4];
+  CUtensorMap maps[5];
   // x [M rows, K] halves, box 64 k x 128 rows, 128-byte swizzle (K-major UMMA layout)
   int rc = encode_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.x, (uint64_t)pb.K, (uint64_t)pb.M,
                                 (uint64_t)pb.ldx * 2, kKC, kMT, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -365,6 +391,12 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   if (rc) return rc;
   rc = encode_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.zeros, (uint64_t)pb.N, (uint64_t)groups,
                             (uint64_t)pb.N * 2, kN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  // out [M rows, N] in boxes of 32 rows x 128 bytes (64 halves or 32 floats), 128-byte swizzle
+  const bool f32 = pb.out_f32 != 0;
+  rc = encode_tensor_map_2d(&maps[4], f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.out,
+                            (uint64_t)pb.N, (uint64_t)pb.M, (uint64_t)pb.ldo * (f32 ? 4 : 2), f32 ? 32 : 64, 32,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   Args a{};
   a.bias = pb.bias;
