@@ -486,8 +486,9 @@ def run_ours(args) -> None:
         max_len = args.prompt + args.warmup + 2 * args.steps + 8
         dec = QwenDecoder(model, batch=args.batch, max_len=max_len,
                           colmajor={"auto": None, "cm": True, "kmajor": False}[args.layout])
-        # prefill in chunks of M <= 32 rows so every projection runs the decode kernel
-        dec.prefill(prompt, chunk=max(1, 32 // args.batch))
+        # the whole prompt in one pass: M = batch x prompt rows per projection
+        # (the tcgen05 GEMM above 128 rows)
+        dec.prefill(prompt)
     dec.capture()
     for _ in range(args.warmup):
         dec.replay()

@@ -9,7 +9,8 @@
 //  * a TMA warp loads, per chunk, the x tiles of the row tiles ([128 rows x
 //    64 k], 128-byte swizzle: the K-major UMMA canonical layout), the packed
 //    weights [32 packed rows x 256 columns] and the chunk's scale/zero rows;
-//  * 4 dequantisation warps turn the packed chunk into a [64 k x 256 n] tile
+//  * 8 dequantisation warps (two per SM sub-partition, so that one hides the
+//    other's latencies) turn the packed chunk into a [64 k x 256 n] tile
 //    of the activation type in shared memory, once for all row tiles, in the
 //    MN-major 128-byte-swizzled UMMA layout, with the reference's rounding:
 //    w = round_x((code - zero) * scale) (quant.py:90-105, reference.py:21-35).
@@ -21,9 +22,11 @@
 //    tiles x 256 columns = all 512 columns) and commits each chunk to an
 //    mbarrier that frees its ring slot. 256 columns per CTA also halve the
 //    re-reads of x against 128-column tiles;
-//  * the 4 dequantisation warps then read the accumulators back with
-//    tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = rows), round to the
-//    activation type, add the bias and round again (reference.py:33-35).
+//  * the 8 dequantisation warps then read the accumulators back with
+//    tcgen05.ld (warp w: TMEM lanes 32 (w % 4) .. + 31 = rows, half of the
+//    columns), round to the activation type, add the bias and round again
+//    (reference.py:33-35), stage the tile in the idle ring and store it with
+//    TMA.
 // Every mbarrier wait is bounded (1 s): on expiry the kernel records an error
 // bit in the workspace header, stops issuing work, waits (bounded) for what is
 // in flight, frees its TMEM and finishes.
@@ -39,7 +42,7 @@ constexpr int kMT = 128;           // rows per row tile (UMMA M)
 constexpr int kMaxTiles = 2;       // row tiles per CTA: 2 x 256 TMEM columns
 constexpr int kKC = 64;            // k per chunk (one 128-byte swizzle atom of halves)
 constexpr int kStages = 3;
-constexpr int kDeqWarps = 4;
+constexpr int kDeqWarps = 8;        // two per SM sub-partition
 constexpr int kThreads = 32 * (kDeqWarps + 2);  // + TMA warp + MMA warp
 
 // stage layout (bytes; the UMMA operand tiles are 1024-byte aligned)
@@ -52,7 +55,10 @@ constexpr int kWBytes = (kKC / 2) * kN;         // 8 KiB
 constexpr int kSOff = kWOff + kWBytes;
 constexpr int kZOff = kSOff + kN * 2;
 constexpr int kStage = ((kZOff + kN * 2) + 1023) / 1024 * 1024;
-static_assert(kStages * kStage >= kDeqWarps * 32768, "the epilogue stages 32 KiB per warp in the ring");
+static_assert(kDeqWarps * 4 == kKC / 2 && 32 * 8 == kN,
+              "dequantisation: 4 packed rows per warp, 8 columns per lane");
+constexpr int kEpiStage = 16384;   // epilogue staging per warp: 32 rows x 128 columns of fp32
+static_assert(kStages * kStage >= kDeqWarps * kEpiStage, "the epilogue stages in the ring");
 
 struct Args {
   const void* bias;
@@ -221,7 +227,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------ dequantisation
-    const int tid = threadIdx.x;  // 0..127
     for (int c = 0; c < n_chunks; ++c) {
       const int slot = c % kStages;
       if (*abort_flag) break;
@@ -230,25 +235,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       uint8_t* st = smem + slot * kStage;
-      const XT* sv = reinterpret_cast<const XT*>(st + kSOff);
-      const XT* zv = reinterpret_cast<const XT*>(st + kZOff);
+      // each lane dequantises columns 8 lane .. 8 lane + 7 in every item: its
+      // scales and (O + zero) offsets are loaded once per chunk
+      const int cg = lane;
+      const uint4 s4 = *reinterpret_cast<const uint4*>(st + kSOff + 16 * cg);
+      const uint4 z4 = *reinterpret_cast<const uint4*>(st + kZOff + 16 * cg);
+      const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
+      uint32_t zlo[4], zhi[4];
 #pragma unroll
-      for (int item = 0; item < 8; ++item) {
-        const int i = tid + 128 * item;
-        const int j = i >> 5;         // packed row: k = 2j, 2j + 1 of the chunk
-        const int cg = i & 31;        // columns 8 cg .. 8 cg + 7
+      for (int p = 0; p < 4; ++p) {
+        zlo[p] = D::add(zw[p], D::off_lo());
+        zhi[p] = D::add(zw[p], D::off_hi());
+      }
+#pragma unroll
+      for (int item = 0; item < 4; ++item) {
+        const int j = warp + kDeqWarps * item;  // packed row: k = 2j, 2j + 1 of the chunk
         const uint2 pw = *reinterpret_cast<const uint2*>(st + kWOff + j * kN + 8 * cg);
-        const uint4 s4 = *reinterpret_cast<const uint4*>(sv + 8 * cg);
-        const uint4 z4 = *reinterpret_cast<const uint4*>(zv + 8 * cg);
-        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
         uint32_t lo[4], hi[4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           // bytes of columns 8cg + 2p, 8cg + 2p + 1 into byte lanes 0 and 2
           const uint32_t word = p < 2 ? pw.x : pw.y;
           const uint32_t tt = __byte_perm(word, 0u, (p & 1) ? 0x4342u : 0x4140u);
-          lo[p] = D::mul(D::sub(D::lo(tt), D::add(zw[p], D::off_lo())), sw[p]);  // k = 2j
-          hi[p] = D::mul(D::sub(D::hi(tt), D::add(zw[p], D::off_hi())), sw[p]);  // k = 2j + 1
+          lo[p] = D::mul(D::sub(D::lo(tt), zlo[p]), sw[p]);  // k = 2j
+          hi[p] = D::mul(D::sub(D::hi(tt), zhi[p]), sw[p]);  // k = 2j + 1
         }
         // MN-major swizzled tile: atom cg / 8 (64 columns), row k, 16-byte chunk (cg % 8) ^ (k % 8)
         uint8_t* b = st + kBOff + (cg >> 3) * 8192;
@@ -264,15 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ------------------------------------------------------------ epilogue
     // Once every MMA has completed, the ring is idle (every copy landed and
-    // was consumed): warp w stages its 32 rows of each row tile there, 32 KiB
-    // per warp, as boxes of [32 rows x 128 bytes] in the 128-byte swizzle
-    // (16-byte chunk c of row r at chunk c ^ (r % 8): conflict-free for
-    // row-per-lane writes), and one lane stores the boxes with TMA (rows and
-    // columns outside the output are not written).
+    // was consumed). Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows of
+    // each row tile; a warp may only read its sub-partition's lane quarter)
+    // and columns 128 (w / 4) .. + 127, stages them in its 16 KiB of the ring
+    // as boxes of [32 rows x 128 bytes] in the 128-byte swizzle (16-byte chunk
+    // c of row r at chunk c ^ (r % 8): conflict-free for row-per-lane writes),
+    // and one lane stores the boxes with TMA (rows and columns outside the
+    // output are not written).
     if (mbar_wait_bounded(accum, 0u, args.err, 8)) {
       tc_fence_after();
       pdl_wait();  // output writes follow the previous kernel
-      uint8_t* stage = smem + warp * 32768;
+      uint8_t* stage = smem + warp * kEpiStage;
+      const int quad = warp & 3, c_base = (warp >> 2) * (kN / 2);
       const int box_cols = args.out_f32 ? 32 : 64;  // columns per 128-byte box row
       const uint32_t rsw = (uint32_t)(lane & 7);
       for (int t = 0; t < tiles; ++t) {
@@ -280,11 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
         }
-        for (int cc = 0; cc < kN; cc += 32) {
+        for (int lc = 0; lc < kN / 2; lc += 32) {
+          const int cc = c_base + lc;
           uint32_t r[32];
-          tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + t * kN + cc, r);
+          tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
           if (args.out_f32) {
-            uint8_t* row = stage + (cc / 32) * 4096 + lane * 128;
+            uint8_t* row = stage + (lc / 32) * 4096 + lane * 128;
 #pragma unroll
             for (int q = 0; q < 8; ++q)
               *reinterpret_cast<uint4*>(row + (((uint32_t)q ^ rsw) << 4)) =
@@ -303,8 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
                          ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
             }
-            uint8_t* row = stage + (cc / 64) * 4096 + lane * 128;
-            const int c0 = (cc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
+            uint8_t* row = stage + (lc / 64) * 4096 + lane * 128;
+            const int c0 = (lc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               *reinterpret_cast<uint4*>(row + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
@@ -315,8 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          const int row0 = m0 + t * kMT + 32 * warp;
-          for (int b = 0; b < kN / box_cols; ++b) tma_store_2d(&omap, stage + b * 4096, n0 + b * box_cols, row0);
+          const int row0 = m0 + t * kMT + 32 * quad;
+          for (int b = 0; b < (kN / 2) / box_cols; ++b)
+            tma_store_2d(&omap, stage + b * 4096, n0 + c_base + b * box_cols, row0);
           bulk_commit_group();
         }
       }
