@@ -677,6 +677,9 @@ def kernel_sweep(args) -> None:
             out_f.write(line + "\n")
             out_f.flush()
 
+    def sk_grid(m, n, k):
+        return int(_lib.load().tf_qlinear_gemm_stream_k_grid(m, n, k))
+
     g = torch.Generator(device=dev).manual_seed(0)
     for dt in (torch.float16, torch.bfloat16):
         dname = "fp16" if dt == torch.float16 else "bf16"
@@ -697,7 +700,7 @@ def kernel_sweep(args) -> None:
                 rec = {"op": "quantized_linear", "dtype": dname, "M": m, "K": k, "N": n, "us": us,
                        "gbs": alg / us / 1e3, "tflops": flops / us / 1e6,
                        "regime": ("gemv" if m <= 32 else f"gemv x {-(-m // 32)} row chunks" if m <= 128
-                                  else "gemm"),
+                                  else "gemm" if not sk_grid(m, n, k) else f"gemm stream-K x {sk_grid(m, n, k)}"),
                        "l2_resident": copies * wbytes < L2}
                 rec["frac_hbm"] = rec["gbs"] / peaks["hbm_gbs"]
                 rec["frac_tensor"] = rec["tflops"] / tflops_peak

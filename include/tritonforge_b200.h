@@ -66,14 +66,25 @@ const char* tf_last_error_message(void);
  * accumulated in fp32, the result is rounded to the activation dtype and the
  * bias (any of fp16/bf16/fp32, or NULL) is added and rounded again -- the
  * rounding points of the reference oracle (reference.py:21-36).
- * `workspace` must hold tf_qlinear_workspace_bytes(...) bytes and be zeroed
- * once before its first use. Word 0 is the error word of the kernels' bounded
+ * `workspace` must hold at least 256 bytes and be zeroed once before its
+ * first use; tf_qlinear_workspace_bytes(...) is the size for the fastest
+ * schedule (above 128 rows the tcgen05 GEMM splits tiles between CTAs when
+ * its tiles would leave SMs idle, and keeps partial tiles there; with less
+ * it runs one tile per CTA). Word 0 is the error word of the kernels' bounded
  * waits: a wait that gives up (1 s) sets a bit there and the call still
  * returns TF_OK, so read it with tf_workspace_error; it stays set until the
  * caller clears it. Calls that share a workspace must be ordered on one
  * stream.
  */
 size_t tf_qlinear_workspace_bytes(int64_t M, int64_t N, int64_t K_pad, int32_t group_size);
+
+/* The tcgen05 GEMM's schedule for an M x N x K problem given a workspace of
+ * tf_qlinear_workspace_bytes: the number of CTAs of its stream-K schedule
+ * (contiguous ranges of (tile, 64-k chunk) units, a split tile finished by
+ * the last CTA to arrive, which adds the pieces in k order), or 0 when it
+ * runs one 256 x 256 tile per CTA. No reference counterpart (the reference
+ * launches one Triton program per output tile, dequant_gemm.py:174-175). */
+int tf_qlinear_gemm_stream_k_grid(int64_t M, int64_t N, int64_t K);
 
 int tf_qlinear(const void* x, int64_t ldx, int x_dtype,
                const uint8_t* packed, const void* scales, const void* zeros, int param_dtype,

@@ -29,7 +29,8 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 
 def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, what: str = "",
-                     max_mismatch: float | None = None, mean_frac: float | None = 0.1) -> dict:
+                     max_mismatch: float | None = None, mean_frac: float | None = 0.1,
+                     pre_bias: np.ndarray | None = None) -> dict:
     """Every element within the contract, max(RMS_TOL x RMS(ref), one ulp of
     the output type at ref): the contract is max-abs <= RMS_TOL x RMS, and a
     difference of one output ulp is the smallest nonzero difference there is
@@ -37,7 +38,13 @@ def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, wha
     fp32 summation-order rounding flip of one large output would otherwise
     fail a correct kernel). Optionally at most `max_mismatch` of the elements
     differ from the oracle at all; the mean abs error is at most `mean_frac`
-    of RMS_TOL x RMS (typical errors are ulp-level, not just bounded)."""
+    of RMS_TOL x RMS (typical errors are ulp-level, not just bounded).
+    `pre_bias` (the oracle's output before its bias add, rounded) allows one
+    summation-order flip at that rounding point: out = round(round(acc) +
+    bias) rounds twice, and a flip of round(acc) by one ulp of acc moves
+    round(acc) + bias by that ulp and can also turn the second rounding the
+    other way (round(acc) + bias is often a tie: two values of one binade add
+    to one extra bit), so the output may differ by ulp(pre_bias) + ulp(out)."""
     got = f32(out)
     ref = np.asarray(ref, np.float32)
     assert got.shape == ref.shape, (got.shape, ref.shape)
@@ -50,8 +57,12 @@ def assert_rms_close(out: torch.Tensor, ref: np.ndarray, dtype: torch.dtype, wha
     assert np.isfinite(got).all(), f"{what}: non-finite output"
     mant = {torch.float16: 11, torch.bfloat16: 8, torch.float32: 24}[dtype]
     ulp = np.ldexp(1.0, np.frexp(np.abs(ref.astype(np.float64)) + 1e-30)[1] - mant)
+    if pre_bias is not None:
+        pre = np.asarray(pre_bias, np.float64)
+        ulp = ulp + np.ldexp(1.0, np.frexp(np.abs(pre) + 1e-30)[1] - mant)
     bad = diff > np.maximum(tol, ulp)
-    assert not bad.any(), (f"{what}: {int(bad.sum())} elements beyond max({RMS_TOL[dtype]} x RMS, 1 ulp); "
+    ulps = "1 ulp" if pre_bias is None else "1 ulp + 1 ulp before the bias"
+    assert not bad.any(), (f"{what}: {int(bad.sum())} elements beyond max({RMS_TOL[dtype]} x RMS, {ulps}); "
                            f"max-abs {err:.4g}, RMS {rms:.4g}")
     mism = float(np.mean(got != ref))
     mean_err = float(np.mean(np.abs(got.astype(np.float64) - ref.astype(np.float64))))

@@ -45,11 +45,23 @@ def test_abi_version_and_status_strings():
 
 
 def test_workspace_sizes_are_sane():
-    # split-K partial sums stay on chip (cluster reduction): the workspace is
-    # the 256-byte header holding the device error word
+    # decode shapes: split-K partial sums stay on chip (cluster reduction), the
+    # workspace is the 256-byte header holding the device error word; the
+    # prefill GEMM's stream-K schedule keeps up to two 256 x 256 fp32 partial
+    # tiles per CTA (148 SMs without a GPU) after 512 bytes, and its arrival
+    # counters (8 per tile, up to 2048 tiles) at the end
     lib = _lib.load()
-    for m, n, k in [(1, 4864, 896), (16, 18944, 3584), (32, 8192, 29568), (2048, 18944, 3584)]:
-        assert 256 <= lib.tf_qlinear_workspace_bytes(m, n, k, 128) <= 1 << 20
+    for m, n, k in [(1, 4864, 896), (16, 18944, 3584), (32, 8192, 29568), (128, 8192, 29568),
+                    (2048, 18944, 3584)]:
+        assert lib.tf_qlinear_workspace_bytes(m, n, k, 128) == 256
+        assert lib.tf_qlinear_gemm_stream_k_grid(m, n, k) == 0
+    for m, n, k in [(512, 3584, 3584), (2048, 1280, 8192)]:
+        grid = lib.tf_qlinear_gemm_stream_k_grid(m, n, k)
+        assert 2 <= grid <= 148
+        tiles = -(-n // 256) * -(-m // 256)
+        partials = 2 * grid * 256 * 256 * 4
+        assert tiles <= 2048
+        assert lib.tf_qlinear_workspace_bytes(m, n, k, 128) == 512 + partials + 2048 * 32
 
 
 def test_c_level_validation_without_gpu():

@@ -265,6 +265,59 @@ def test_gemm_regime(m, n, k, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", [(512, 3584, 3584), (300, 1008, 4096), (1024, 1536, 18944), (512, 512, 3584)])
+def test_gemm_stream_k(m, n, k, dtype):
+    """Shapes whose 256 x 256 tiles would leave SMs idle run the stream-K
+    schedule (tiles split between CTAs, the pieces added in k order by the
+    last CTA to arrive): sampled rows against the oracle, bit-identical across
+    launches, and within the contract with a header-only workspace (which
+    runs one tile per CTA)."""
+    lib = _lib.load()
+    assert lib.tf_qlinear_gemm_stream_k_grid(m, n, k) > 0
+    x, packed, scales, zeros, b = _linear_inputs(m, n, k, dtype, w_std=0.02, seed=m + n)
+    out = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemm"})
+    rows = torch.randperm(m, generator=torch.Generator().manual_seed(2))[:64].sort().values
+    rows = torch.cat([rows, torch.tensor([m - 1])]).unique().cuda()
+    ref = oracle_linear(x[rows], packed, scales, zeros, b)
+    pre = oracle_linear(x[rows], packed, scales, zeros, None)
+    assert_rms_close(out[rows], ref, dtype, f"stream-K gemm {m}x{n}x{k}", pre_bias=pre)
+    for _ in range(2):
+        again = kernels.quantized_linear(x, packed, scales, zeros, b, config={"regime": "gemm"})
+        assert torch.equal(out, again), "deterministic"
+    ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    dp = torch.full_like(out, float("nan"))
+    _lib.check(lib.tf_qlinear_ex(x.data_ptr(), x.stride(0), _lib.dtype_code(dtype), packed.data_ptr(),
+                                 scales.data_ptr(), zeros.data_ptr(), _lib.dtype_code(dtype), b.data_ptr(),
+                                 _lib.dtype_code(dtype), dp.data_ptr(), n, m, n, k, k, GROUP, ws.data_ptr(),
+                                 ws.numel(), _lib.REGIME_GEMM, _lib.stream_ptr(x.device)), "qlinear_ex")
+    assert_rms_close(dp[rows], ref, dtype, f"data-parallel gemm {m}x{n}x{k}", pre_bias=pre)
+    assert torch.isfinite(dp).all()
+    assert _lib.workspaces.errors(x.device) == 0 and int(ws[:4].view(torch.int32).item()) == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 3584, 3584), (2048, 1280, 8192)])
+def test_gemm_stream_k_partial_is_the_unrounded_sum(m, n, k):
+    """tf_qlinear_partial (a row-parallel shard's fp32 partial) on the
+    stream-K schedule: finite everywhere, and rounded once equal bit for bit
+    to the regular entry point's output on the same schedule."""
+    dtype = torch.bfloat16
+    lib = _lib.load()
+    assert lib.tf_qlinear_gemm_stream_k_grid(m, n, k) > 0
+    x, packed, scales, zeros, _ = _linear_inputs(m, n, k, dtype, w_std=0.02, bias=False, seed=k)
+    want = kernels.quantized_linear(x, packed, scales, zeros, None, GROUP)
+    ws = _lib.workspaces.get(x.device, lib.tf_qlinear_workspace_bytes(m, n, k, GROUP))
+    part = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    _lib.check(lib.tf_qlinear_partial(x.data_ptr(), k, _lib.BF16, packed.data_ptr(), scales.data_ptr(),
+                                      zeros.data_ptr(), _lib.BF16, part.data_ptr(), n, m, n, k, k, GROUP,
+                                      ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device)), "qlinear_partial")
+    torch.cuda.synchronize()
+    assert torch.isfinite(part).all()
+    assert torch.equal(part.to(dtype), want)
+    rows = torch.tensor([0, m // 2, m - 1]).cuda()
+    assert_rms_close(want[rows], oracle_linear(x[rows], packed, scales, zeros, None), dtype, "stream-K partial")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("m,n,k", [(33, 512, 896), (64, 3584, 3584), (100, 256, 1024), (128, 896, 4864)])
 def test_auto_regime_between_33_and_128_rows(m, n, k, dtype):
     """The automatic regime runs 33..128 rows as 32-row chunks of the decode

@@ -6,8 +6,12 @@
 namespace tf {
 
 // Workspace layout: [0, 256) header, word 0 = device error bits of bounded
-// waits. The kernels keep all other scratch on chip.
+// waits; [256, 512) the head kernels' counter; from 512 the prefill GEMM's
+// stream-K partial tiles, and in the last 64 KiB its arrival counters (zero
+// between launches). Every kernel runs with the header alone (the GEMM then
+// takes its data-parallel schedule).
 constexpr size_t kWsHeader = 256;
+inline size_t qlinear_min_workspace_bytes() { return kWsHeader; }
 
 struct QLinearProblem {
   const void* x;

@@ -18,10 +18,12 @@
 //
 // All calls share the one array and it keeps whatever the last call left in
 // it: calls whose kernels can overlap on the GPU (different streams without an
-// ordering between them) race on it, so order them on one stream. Problems
-// whose workspace (tf_qlinear_workspace_bytes) is larger than the array are
-// rejected with TF_ERR_WORKSPACE. Nothing here calls cudaMalloc, cudaFree or
-// any allocating library routine.
+// ordering between them) race on it, so order them on one stream. Every
+// regime runs within the array: the kernels need only the 256-byte header,
+// and the prefill GEMM's stream-K schedule, whose scratch
+// (tf_qlinear_workspace_bytes) is larger, falls back to its data-parallel
+// schedule here. Nothing here calls cudaMalloc, cudaFree or any allocating
+// library routine.
 //
 // Word 0 of the array is the error word of the kernels' bounded waits, as in a
 // caller's workspace: a wait that gives up (after 1 s) sets a bit there and the
@@ -81,7 +83,7 @@ extern "C" int tf_qlinear_noalloc(const void* x, int64_t ldx, int x_dtype, const
                                   int bias_dtype, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
                                   int64_t K_pad, int32_t group_size, void* stream) {
   using namespace tf;
-  const size_t need = tf_qlinear_workspace_bytes(M, N, K_pad, group_size);
+  const size_t need = qlinear_min_workspace_bytes();
   if (need > kNoAllocScratchBytes)
     return fail(TF_ERR_WORKSPACE,
                 "qlinear_noalloc: this problem needs %zu bytes of scratch, more than the %zu-byte static "

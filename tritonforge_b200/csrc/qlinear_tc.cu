@@ -71,6 +71,17 @@ struct Args {
   int bias_dtype;
   uint32_t idesc;      // tcgen05 instruction descriptor
   int out_f32;         // store the fp32 sums unrounded (a row-parallel partial, no bias)
+  // Schedule. Tiles of 256 columns x 256 rows, column-fastest; a unit is one
+  // 64-k chunk of one tile. Data-parallel (stream_k = 0): the grid is
+  // (column tiles, row groups) and each CTA runs one whole tile. Stream-K
+  // (stream_k = 1): gridDim.x CTAs each run a contiguous range of the
+  // n_tiles x n_chunks units; a tile split between CTAs is finished by the
+  // last of them to arrive, which adds the pieces in k order.
+  int tiles_n;
+  int n_tiles;
+  int stream_k;
+  int* counters;       // stream-K: arrivals per warp region of each tile (zero between launches)
+  float* partials;     // stream-K: 2 partial tiles per CTA, [64 column quads][256 rows][4 columns]
 };
 
 template <typename T> struct Deq;
@@ -119,6 +130,39 @@ template <> struct Deq<__nv_bfloat16> {
   }
 };
 
+// Units [u_begin, u_end) of the stream-K schedule belong to CTA g: an even
+// split of the units over the grid; cta_of(u) inverts it.
+struct Sched {
+  int64_t total;
+  int grid;
+  __device__ __forceinline__ int64_t bound(int g) const { return (int64_t)g * total / grid; }
+  __device__ __forceinline__ int cta_of(int64_t u) const { return (int)(((u + 1) * grid - 1) / total); }
+};
+
+// One segment of a CTA's work: chunks [cb, ce) of tile `tile`.
+struct Seg {
+  int tile, cb, ce, n0, m0, tiles;
+};
+
+__device__ __forceinline__ bool next_seg(const Args& a, int64_t& u, int64_t u_end, Seg& sg) {
+  if (u >= u_end) return false;
+  const int nc = a.n_chunks;
+  sg.tile = (int)(u / nc);
+  sg.cb = (int)(u % nc);
+  const int64_t left = u_end - u;
+  sg.ce = left < (int64_t)(nc - sg.cb) ? sg.cb + (int)left : nc;
+  u += sg.ce - sg.cb;
+  sg.n0 = (sg.tile % a.tiles_n) * kN;
+  sg.m0 = (sg.tile / a.tiles_n) * (kMT * kMaxTiles);
+  const int rows = (a.M - sg.m0 + kMT - 1) / kMT;
+  sg.tiles = rows < kMaxTiles ? rows : kMaxTiles;
+  return true;
+}
+
+__device__ __forceinline__ void deq_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kDeqWarps * 32) : "memory");
+}
+
 template <typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
@@ -130,17 +174,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);  // TMA bytes landed
   uint64_t* bready = full + kStages;                                      // dequantised tile written
   uint64_t* freed = bready + kStages;                                     // MMAs of the slot done
-  uint64_t* accum = freed + kStages;                                      // all MMAs done
-  uint64_t* alldone = accum + 1;                                          // every warp finished its role
+  uint64_t* accum = freed + kStages;                                      // a segment's MMAs done
+  uint64_t* epi_done = accum + 1;                                         // a segment's epilogue done
+  uint64_t* alldone = epi_done + 1;                                       // every warp finished its role
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(alldone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kN;
-  const int m0 = blockIdx.y * kMT * kMaxTiles;
-  int tiles = (args.M - m0 + kMT - 1) / kMT;
-  if (tiles > kMaxTiles) tiles = kMaxTiles;
-  const int n_chunks = args.n_chunks;
+  const int nc = args.n_chunks;
+  const Sched sched{(int64_t)args.n_tiles * nc, (int)gridDim.x};
+  int64_t u_begin, u_end;
+  if (args.stream_k) {
+    u_begin = sched.bound(blockIdx.x);
+    u_end = sched.bound(blockIdx.x + 1);
+  } else {
+    u_begin = (int64_t)(blockIdx.y * args.tiles_n + blockIdx.x) * nc;
+    u_end = u_begin + nc;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -149,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&freed[i], 1);
     }
     mbar_init(accum, 1);
+    mbar_init(epi_done, kDeqWarps);
     mbar_init(alldone, kThreads / 32);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -173,135 +224,234 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&smap);
       prefetch_tensormap(&zmap);
       pdl_wait();
-      const uint32_t tx = (uint32_t)(tiles * kXTile + kWBytes + 2 * kN * 2);
-      int issued = 0;
-      for (int c = 0; c < n_chunks; ++c) {
-        const int slot = c % kStages;
-        if (c >= kStages && !mbar_wait_bounded(&freed[slot], (uint32_t)(c / kStages - 1) & 1u, args.err, 1)) {
+      int it = 0, issued = 0, seg = 0;
+      Seg sg;
+      for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+        // the previous segment's epilogue stages its tile in the ring
+        if (seg > 0 && !mbar_wait_bounded(epi_done, (uint32_t)(seg - 1) & 1u, args.err, 1)) {
           *abort_flag = 1;
           break;
         }
-        if (*abort_flag) break;
-        uint8_t* st = smem + slot * kStage;
-        mbar_arrive_expect_tx(&full[slot], tx);
-        for (int t = 0; t < tiles; ++t) tma_load_2d(st + kXOff + t * kXTile, &xmap, &full[slot], c * kKC, m0 + t * kMT);
-        tma_load_2d(st + kWOff, &wmap, &full[slot], n0, c * (kKC / 2));
-        const int grow = (c * kKC) / args.group_size;
-        tma_load_2d(st + kSOff, &smap, &full[slot], n0, grow);
-        tma_load_2d(st + kZOff, &zmap, &full[slot], n0, grow);
-        issued = c + 1;
+        const uint32_t tx = (uint32_t)(sg.tiles * kXTile + kWBytes + 2 * kN * 2);
+        for (int c = sg.cb; c < sg.ce; ++c, ++it) {
+          const int slot = it % kStages;
+          if (it >= kStages && !mbar_wait_bounded(&freed[slot], (uint32_t)(it / kStages - 1) & 1u, args.err, 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          uint8_t* st = smem + slot * kStage;
+          mbar_arrive_expect_tx(&full[slot], tx);
+          for (int t = 0; t < sg.tiles; ++t)
+            tma_load_2d(st + kXOff + t * kXTile, &xmap, &full[slot], c * kKC, sg.m0 + t * kMT);
+          tma_load_2d(st + kWOff, &wmap, &full[slot], sg.n0, c * (kKC / 2));
+          const int grow = (c * kKC) / args.group_size;
+          tma_load_2d(st + kSOff, &smap, &full[slot], sg.n0, grow);
+          tma_load_2d(st + kZOff, &zmap, &full[slot], sg.n0, grow);
+          issued = it + 1;
+        }
       }
-      if (*abort_flag) {
-        for (int c = (issued > kStages ? issued - kStages : 0); c < issued; ++c)
-          mbar_wait_bounded(&full[c % kStages], (uint32_t)(c / kStages) & 1u, args.err, 4);
+      if (*abort_flag) {  // the copies in flight land before the CTA exits
+        for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
+          mbar_wait_bounded(&full[i % kStages], (uint32_t)(i / kStages) & 1u, args.err, 4);
       }
     }
   } else if (warp == kDeqWarps + 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      for (int c = 0; c < n_chunks; ++c) {
-        const int slot = c % kStages;
-        const uint32_t ph = (uint32_t)(c / kStages) & 1u;
-        if (*abort_flag) break;
-        if (!mbar_wait_bounded(&full[slot], ph, args.err, 2) || !mbar_wait_bounded(&bready[slot], ph, args.err, 2)) {
+      int it = 0, seg = 0;
+      Seg sg;
+      for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+        // the previous segment's epilogue has read the accumulators
+        if (seg > 0 && !mbar_wait_bounded(epi_done, (uint32_t)(seg - 1) & 1u, args.err, 2)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + slot * kStage);
-#pragma unroll
-        for (int ks = 0; ks < kKC / 16; ++ks) {
-          // B: MN-major, atoms of 64 n x 8 k rows (1 KiB); next 8 k rows +1 KiB (SBO),
-          // next 64 n +8 KiB (LBO); a 16-k step starts 2 KiB further
-          const uint64_t bdesc = umma_desc(st + kBOff + ks * 2048, 8192, 1024);
-          for (int t = 0; t < tiles; ++t) {
-            // A: K-major rows of 128 B, 8-row atoms 1 KiB apart (SBO); a 16-k step is 32 B
-            const uint64_t adesc = umma_desc(st + kXOff + t * kXTile + ks * 32, 16, 1024);
-            umma_f16(tmem + t * kN, adesc, bdesc, args.idesc, (c > 0 || ks > 0) ? 1u : 0u);
+        for (int c = sg.cb; c < sg.ce; ++c, ++it) {
+          const int slot = it % kStages;
+          const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+          if (*abort_flag) break;
+          if (!mbar_wait_bounded(&full[slot], ph, args.err, 2) || !mbar_wait_bounded(&bready[slot], ph, args.err, 2)) {
+            *abort_flag = 1;
+            break;
           }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + slot * kStage);
+#pragma unroll
+          for (int ks = 0; ks < kKC / 16; ++ks) {
+            // B: MN-major, atoms of 64 n x 8 k rows (1 KiB); next 8 k rows +1 KiB (SBO),
+            // next 64 n +8 KiB (LBO); a 16-k step starts 2 KiB further
+            const uint64_t bdesc = umma_desc(st + kBOff + ks * 2048, 8192, 1024);
+            for (int t = 0; t < sg.tiles; ++t) {
+              // A: K-major rows of 128 B, 8-row atoms 1 KiB apart (SBO); a 16-k step is 32 B
+              const uint64_t adesc = umma_desc(st + kXOff + t * kXTile + ks * 32, 16, 1024);
+              umma_f16(tmem + t * kN, adesc, bdesc, args.idesc, (c > sg.cb || ks > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&freed[slot]);
         }
-        umma_commit(&freed[slot]);
+        if (*abort_flag) break;
+        umma_commit(accum);  // arrives once every MMA of the segment has completed
       }
-      umma_commit(accum);  // arrives once every MMA issued above has completed
-      mbar_wait_bounded(accum, 0u, args.err, 8);  // this warp reports done only after them
+      // this warp reports done only after its last MMAs
+      if (!*abort_flag && seg > 0) mbar_wait_bounded(accum, (uint32_t)(seg - 1) & 1u, args.err, 8);
     }
   } else {
     // ------------------------------------------------------ dequantisation
-    for (int c = 0; c < n_chunks; ++c) {
-      const int slot = c % kStages;
+    const int quad = warp & 3, c_base = (warp >> 2) * (kN / 2);
+    const uint32_t rsw = (uint32_t)(lane & 7);
+    uint8_t* stage = smem + warp * kEpiStage;
+    int it = 0, seg = 0;
+    Seg sg;
+    for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+      for (int c = sg.cb; c < sg.ce; ++c, ++it) {
+        const int slot = it % kStages;
+        if (*abort_flag) break;
+        if (!mbar_wait_bounded(&full[slot], (uint32_t)(it / kStages) & 1u, args.err, 2)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + slot * kStage;
+        // each lane dequantises columns 8 lane .. 8 lane + 7 in every item: its
+        // scales and (O + zero) offsets are loaded once per chunk
+        const int cg = lane;
+        const uint4 s4 = *reinterpret_cast<const uint4*>(st + kSOff + 16 * cg);
+        const uint4 z4 = *reinterpret_cast<const uint4*>(st + kZOff + 16 * cg);
+        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
+        uint32_t zlo[4], zhi[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          zlo[p] = D::add(zw[p], D::off_lo());
+          zhi[p] = D::add(zw[p], D::off_hi());
+        }
+#pragma unroll
+        for (int item = 0; item < 4; ++item) {
+          const int j = warp + kDeqWarps * item;  // packed row: k = 2j, 2j + 1 of the chunk
+          const uint2 pw = *reinterpret_cast<const uint2*>(st + kWOff + j * kN + 8 * cg);
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            // bytes of columns 8cg + 2p, 8cg + 2p + 1 into byte lanes 0 and 2
+            const uint32_t word = p < 2 ? pw.x : pw.y;
+            const uint32_t tt = __byte_perm(word, 0u, (p & 1) ? 0x4342u : 0x4140u);
+            lo[p] = D::mul(D::sub(D::lo(tt), zlo[p]), sw[p]);  // k = 2j
+            hi[p] = D::mul(D::sub(D::hi(tt), zhi[p]), sw[p]);  // k = 2j + 1
+          }
+          // MN-major swizzled tile: atom cg / 8 (64 columns), row k, 16-byte chunk (cg % 8) ^ (k % 8)
+          uint8_t* b = st + kBOff + (cg >> 3) * 8192;
+          const int k0 = 2 * j, k1 = 2 * j + 1;
+          *reinterpret_cast<uint4*>(b + k0 * 128 + (((cg & 7) ^ (k0 & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(b + k1 * 128 + (((cg & 7) ^ (k1 & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+        // make the generic-proxy stores visible to the tensor core, then signal
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[slot]);
+      }
       if (*abort_flag) break;
-      if (!mbar_wait_bounded(&full[slot], (uint32_t)(c / kStages) & 1u, args.err, 2)) {
+      if (!mbar_wait_bounded(accum, (uint32_t)seg & 1u, args.err, 8)) {
         *abort_flag = 1;
         break;
       }
-      uint8_t* st = smem + slot * kStage;
-      // each lane dequantises columns 8 lane .. 8 lane + 7 in every item: its
-      // scales and (O + zero) offsets are loaded once per chunk
-      const int cg = lane;
-      const uint4 s4 = *reinterpret_cast<const uint4*>(st + kSOff + 16 * cg);
-      const uint4 z4 = *reinterpret_cast<const uint4*>(st + kZOff + 16 * cg);
-      const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
-      uint32_t zlo[4], zhi[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        zlo[p] = D::add(zw[p], D::off_lo());
-        zhi[p] = D::add(zw[p], D::off_hi());
-      }
-#pragma unroll
-      for (int item = 0; item < 4; ++item) {
-        const int j = warp + kDeqWarps * item;  // packed row: k = 2j, 2j + 1 of the chunk
-        const uint2 pw = *reinterpret_cast<const uint2*>(st + kWOff + j * kN + 8 * cg);
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          // bytes of columns 8cg + 2p, 8cg + 2p + 1 into byte lanes 0 and 2
-          const uint32_t word = p < 2 ? pw.x : pw.y;
-          const uint32_t tt = __byte_perm(word, 0u, (p & 1) ? 0x4342u : 0x4140u);
-          lo[p] = D::mul(D::sub(D::lo(tt), zlo[p]), sw[p]);  // k = 2j
-          hi[p] = D::mul(D::sub(D::hi(tt), zhi[p]), sw[p]);  // k = 2j + 1
-        }
-        // MN-major swizzled tile: atom cg / 8 (64 columns), row k, 16-byte chunk (cg % 8) ^ (k % 8)
-        uint8_t* b = st + kBOff + (cg >> 3) * 8192;
-        const int k0 = 2 * j, k1 = 2 * j + 1;
-        *reinterpret_cast<uint4*>(b + k0 * 128 + (((cg & 7) ^ (k0 & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(b + k1 * 128 + (((cg & 7) ^ (k1 & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      }
-      // make the generic-proxy stores visible to the tensor core, then signal
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bready[slot]);
-    }
-
-    // ------------------------------------------------------------ epilogue
-    // Once every MMA has completed, the ring is idle (every copy landed and
-    // was consumed). Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows of
-    // each row tile; a warp may only read its sub-partition's lane quarter)
-    // and columns 128 (w / 4) .. + 127, stages them in its 16 KiB of the ring
-    // as boxes of [32 rows x 128 bytes] in the 128-byte swizzle (16-byte chunk
-    // c of row r at chunk c ^ (r % 8): conflict-free for row-per-lane writes),
-    // and one lane stores the boxes with TMA (rows and columns outside the
-    // output are not written).
-    if (mbar_wait_bounded(accum, 0u, args.err, 8)) {
       tc_fence_after();
-      pdl_wait();  // output writes follow the previous kernel
-      uint8_t* stage = smem + warp * kEpiStage;
-      const int quad = warp & 3, c_base = (warp >> 2) * (kN / 2);
+      pdl_wait();  // output and scratch writes follow the previous kernel
+
+      // -------------------------------------------------------- epilogue
+      // Warp w owns a region of the tile: TMEM lanes 32 (w % 4) .. + 31 of each
+      // row tile (a warp may only read its sub-partition's lane quarter) and
+      // columns 128 (w / 4) .. + 127.
+      const bool whole = sg.cb == 0 && sg.ce == nc;
+      int n_pieces = 1, first_cta = 0, end_slot = 1;
+      float* own_part = nullptr;
+      if (!whole) {
+        // a piece of a split tile: this region's fp32 sums go to this CTA's
+        // partial slot (lane = row: 16-byte stores of 32 lanes are contiguous)
+        const int64_t a0 = (int64_t)sg.tile * nc;
+        first_cta = sched.cta_of(a0);
+        n_pieces = sched.cta_of(a0 + nc - 1) - first_cta + 1;
+        // Piece p of the tile comes from CTA first_cta + p, whose segment here
+        // is its last one (slot 2g + 1) except possibly for the final piece,
+        // which is that CTA's first segment and also its last only if its
+        // range ends with the tile (slot 2g otherwise).
+        end_slot = sched.bound(first_cta + n_pieces) <= a0 + nc ? 1 : 0;
+        const bool last_seg = u_end <= a0 + nc;
+        own_part = args.partials + (size_t)(2 * blockIdx.x + (last_seg ? 1 : 0)) * (kMT * kMaxTiles * kN);
+        for (int t = 0; t < sg.tiles; ++t) {
+          const int row = t * kMT + 32 * quad + lane;
+          for (int lc = 0; lc < kN / 2; lc += 32) {
+            const int cc = c_base + lc;
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              __stcg(reinterpret_cast<float4*>(own_part) + (size_t)(cc / 4 + q) * (kMT * kMaxTiles) + row,
+                     make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
+          }
+        }
+        __syncwarp();
+        __threadfence();
+        __syncwarp();
+        int before = 0;
+        if (lane == 0) before = atomicAdd(&args.counters[sg.tile * kDeqWarps + warp], 1);
+        before = __shfl_sync(0xffffffffu, before, 0);
+        if (before != n_pieces - 1) {
+          // another CTA finishes this region
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(epi_done);
+          continue;
+        }
+        __threadfence();  // every other piece of the region is visible
+        if (lane == 0) args.counters[sg.tile * kDeqWarps + warp] = 0;  // ready for the next launch
+      }
+      // The region's fp32 sums (a whole tile's, or the pieces of a split tile
+      // added in k order) are rounded (plus bias) or kept as fp32, staged in
+      // this warp's 16 KiB of the idle ring as boxes of [32 rows x 128 bytes]
+      // in the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8):
+      // conflict-free for row-per-lane writes) and stored by one lane with TMA
+      // (rows and columns outside the output are not written).
       const int box_cols = args.out_f32 ? 32 : 64;  // columns per 128-byte box row
-      const uint32_t rsw = (uint32_t)(lane & 7);
-      for (int t = 0; t < tiles; ++t) {
+      for (int t = 0; t < sg.tiles; ++t) {
         if (t > 0) {  // the previous tile's stores have read the staging area
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
         }
+        const int row = t * kMT + 32 * quad + lane;
         for (int lc = 0; lc < kN / 2; lc += 32) {
           const int cc = c_base + lc;
           uint32_t r[32];
-          tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
+          if (whole) {
+            tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
+          } else {
+            // every piece from the partial slots (this CTA's own included), in k order
+            float acc[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+#pragma unroll 1
+            for (int p = 0; p < n_pieces; ++p) {
+              const int g = first_cta + p;
+              const float4* part = reinterpret_cast<const float4*>(
+                  args.partials + (size_t)(2 * g + (p == n_pieces - 1 ? end_slot : 1)) * (kMT * kMaxTiles * kN)) +
+                  (size_t)(cc / 4) * (kMT * kMaxTiles) + row;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 f = __ldcg(part + q * (kMT * kMaxTiles));
+                acc[4 * q] += f.x;
+                acc[4 * q + 1] += f.y;
+                acc[4 * q + 2] += f.z;
+                acc[4 * q + 3] += f.w;
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(acc[e]);
+          }
           if (args.out_f32) {
-            uint8_t* row = stage + (lc / 32) * 4096 + lane * 128;
+            uint8_t* srow = stage + (lc / 32) * 4096 + lane * 128;
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4*>(row + (((uint32_t)q ^ rsw) << 4)) =
+              *reinterpret_cast<uint4*>(srow + (((uint32_t)q ^ rsw) << 4)) =
                   make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
           } else {
             uint32_t h[16];
@@ -309,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 32; e += 2) {
               float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
               if (args.bias) {
-                const int col = n0 + cc + e;
+                const int col = sg.n0 + cc + e;
                 if (col < args.N) v0 += load_as_f32(args.bias, col, args.bias_dtype);
                 if (col + 1 < args.N) v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
               }
@@ -317,11 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
                          ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
             }
-            uint8_t* row = stage + (lc / 64) * 4096 + lane * 128;
+            uint8_t* srow = stage + (lc / 64) * 4096 + lane * 128;
             const int c0 = (lc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(row + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
+              *reinterpret_cast<uint4*>(srow + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
                   make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
           }
         }
@@ -329,14 +479,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          const int row0 = m0 + t * kMT + 32 * quad;
+          const int row0 = sg.m0 + t * kMT + 32 * quad;
           for (int b = 0; b < (kN / 2) / box_cols; ++b)
-            tma_store_2d(&omap, stage + b * 4096, n0 + c_base + b * box_cols, row0);
+            tma_store_2d(&omap, stage + b * 4096, sg.n0 + c_base + b * box_cols, row0);
           bulk_commit_group();
         }
       }
-      if (lane == 0) bulk_wait_all();  // the output is written before this CTA reports done
+      if (lane == 0) bulk_wait_all();  // written (and the staging area free) before the ring is reused
+      tc_fence_before();
       __syncwarp();
+      if (lane == 0) mbar_arrive(epi_done);
     }
   }
   // Teardown: the TMA and MMA warps diverge (one lane works), and an aligned
@@ -368,7 +520,68 @@ bool gemm_supported(const QLinearProblem& pb) {
   return true;
 }
 
-size_t gemm_workspace_bytes(int64_t, int64_t, int64_t) { return kWsHeader; }
+namespace {
+
+// Stream-K plan for an M x N x K problem: the grid (0 = data-parallel) and
+// the workspace it needs. Costs are in chunk times (one 64-k chunk of one
+// 256 x 256 tile, ~0.7 us): a data-parallel wave costs its chunks plus an
+// epilogue (~10 chunks); stream-K costs an even share of all chunks plus up
+// to two partial epilogues and one output epilogue, plus the reads of the
+// other pieces of a split tile by the CTA that finishes it (a 256 KiB fp32
+// piece per ~14 chunk times, measured), and is taken when it saves 15% or
+// more.
+struct SkPlan {
+  int grid;
+  int64_t n_tiles;
+  size_t bytes;
+};
+
+constexpr int64_t kEpiChunks = 10;
+constexpr int64_t kPieceReadChunks = 14;
+constexpr int64_t kMinChunksPerCta = 16;
+constexpr size_t kSkOff = 512;  // partial tiles: after the header and the head kernels' counter
+// Arrival counters (one per warp region of a tile) live in the last bytes of
+// the workspace, a region no other kernel writes: they start at zero (a new
+// workspace is zeroed) and the last arrival at each region puts it back.
+constexpr int64_t kSkMaxTiles = 2048;
+constexpr size_t kSkCounterBytes = (size_t)kSkMaxTiles * tc::kDeqWarps * sizeof(int);
+
+SkPlan sk_plan(int64_t M, int64_t N, int64_t K) {
+  using namespace tc;
+  SkPlan p{0, 0, kWsHeader};
+  const int64_t nc = K / kKC;
+  p.n_tiles = cdiv(N, (int64_t)kN) * cdiv(M, (int64_t)kMT * kMaxTiles);
+  const int64_t sms = num_sms();
+  // up to 128 rows the automatic regime runs the decode GEMV, not this kernel
+  if (M <= 128 || nc <= 0 || sms <= 0 || p.n_tiles > kSkMaxTiles) return p;
+  const int64_t total = p.n_tiles * nc;
+  int64_t grid = total / kMinChunksPerCta;
+  if (grid > sms) grid = sms;
+  if (grid < 2) return p;
+  const int64_t per_cta = cdiv(total, grid);
+  const int64_t pieces = per_cta >= nc ? 2 : cdiv(nc, per_cta) + 1;
+  const int64_t dp = cdiv(p.n_tiles, sms) * (nc + kEpiChunks);
+  const int64_t sk = per_cta + 3 * kEpiChunks + kPieceReadChunks * (pieces - 1);
+  if (sk * 100 > dp * 85) return p;
+  p.grid = (int)grid;
+  p.bytes = kSkOff + (size_t)2 * grid * (kMT * kMaxTiles) * kN * sizeof(float) + kSkCounterBytes;
+  return p;
+}
+
+}  // namespace
+
+// The fastest schedule's scratch; any workspace of at least the header works
+// (a smaller one runs the data-parallel schedule).
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad) { return sk_plan(M, N, K_pad).bytes; }
+
+}  // namespace tf
+
+extern "C" int tf_qlinear_gemm_stream_k_grid(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return tf::sk_plan(M, N, K).grid;
+}
+
+namespace tf {
 
 template <typename XT>
 static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
@@ -429,7 +642,17 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   // B MN-major (bit 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28)
   a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (1u << 16) | ((uint32_t)(kN >> 3) << 17) |
             ((uint32_t)(kMT >> 4) << 24);
-  const dim3 grid((unsigned)cdiv(pb.N, kN), (unsigned)cdiv(pb.M, (int64_t)kMT * kMaxTiles));
+  a.tiles_n = (int)cdiv(pb.N, (int64_t)kN);
+  dim3 grid((unsigned)a.tiles_n, (unsigned)cdiv(pb.M, (int64_t)kMT * kMaxTiles));
+  const SkPlan plan = sk_plan(pb.M, pb.N, pb.K);
+  a.n_tiles = (int)plan.n_tiles;
+  if (plan.grid > 0 && pb.workspace_bytes >= plan.bytes && aligned(pb.workspace, 16)) {
+    uint8_t* ws = static_cast<uint8_t*>(pb.workspace);
+    a.stream_k = 1;
+    a.partials = reinterpret_cast<float*>(ws + kSkOff);
+    a.counters = reinterpret_cast<int*>(ws + ((pb.workspace_bytes - kSkCounterBytes) & ~(size_t)15));
+    grid = dim3((unsigned)plan.grid, 1);
+  }
   if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16>(grid, maps, a, st);
   return launch_gemm<__half>(grid, maps, a, st);
 }
