@@ -52,10 +52,10 @@ def test_workspace_sizes_are_sane():
     # counters (8 per tile, up to 2048 tiles) at the end
     lib = _lib.load()
     for m, n, k in [(1, 4864, 896), (16, 18944, 3584), (32, 8192, 29568), (128, 8192, 29568),
-                    (2048, 18944, 3584)]:
+                    (2048, 18944, 3584), (2048, 3584, 3584)]:
         assert lib.tf_qlinear_workspace_bytes(m, n, k, 128) == 256
         assert lib.tf_qlinear_gemm_stream_k_grid(m, n, k) == 0
-    for m, n, k in [(512, 3584, 3584), (2048, 1280, 8192)]:
+    for m, n, k in [(512, 3584, 18944), (300, 1008, 18944), (2048, 1280, 8192)]:
         grid = lib.tf_qlinear_gemm_stream_k_grid(m, n, k)
         assert 2 <= grid <= 148
         tiles = -(-n // 256) * -(-m // 256)

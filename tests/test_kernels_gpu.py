@@ -265,7 +265,7 @@ def test_gemm_regime(m, n, k, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("m,n,k", [(512, 3584, 3584), (300, 1008, 4096), (1024, 1536, 18944), (512, 512, 3584)])
+@pytest.mark.parametrize("m,n,k", [(512, 3584, 18944), (300, 1008, 18944), (300, 256, 16384), (1024, 2048, 8192)])
 def test_gemm_stream_k(m, n, k, dtype):
     """Shapes whose 256 x 256 tiles would leave SMs idle run the stream-K
     schedule (tiles split between CTAs, the pieces added in k order by the
@@ -295,7 +295,7 @@ def test_gemm_stream_k(m, n, k, dtype):
     assert _lib.workspaces.errors(x.device) == 0 and int(ws[:4].view(torch.int32).item()) == 0
 
 
-@pytest.mark.parametrize("m,n,k", [(512, 3584, 3584), (2048, 1280, 8192)])
+@pytest.mark.parametrize("m,n,k", [(512, 1024, 8192), (2048, 1280, 8192)])
 def test_gemm_stream_k_partial_is_the_unrounded_sum(m, n, k):
     """tf_qlinear_partial (a row-parallel shard's fp32 partial) on the
     stream-K schedule: finite everywhere, and rounded once equal bit for bit

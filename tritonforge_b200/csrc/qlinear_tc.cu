@@ -72,11 +72,12 @@ struct Args {
   uint32_t idesc;      // tcgen05 instruction descriptor
   int out_f32;         // store the fp32 sums unrounded (a row-parallel partial, no bias)
   // Schedule. Tiles of 256 columns x 256 rows, column-fastest; a unit is one
-  // 64-k chunk of one tile. Data-parallel (stream_k = 0): the grid is
-  // (column tiles, row groups) and each CTA runs one whole tile. Stream-K
-  // (stream_k = 1): gridDim.x CTAs each run a contiguous range of the
-  // n_tiles x n_chunks units; a tile split between CTAs is finished by the
-  // last of them to arrive, which adds the pieces in k order.
+  // 64-k chunk of one tile. Data-parallel (stream_k = 0, the kernel built
+  // without kSK): the grid is (column tiles, row groups) and each CTA runs
+  // one whole tile. Stream-K (stream_k = 1, kSK): gridDim.x CTAs each run a
+  // contiguous range of the n_tiles x n_chunks units; a tile split between
+  // CTAs is finished by the last of them to arrive, which adds the pieces in
+  // k order.
   int tiles_n;
   int n_tiles;
   int stream_k;
@@ -159,11 +160,35 @@ __device__ __forceinline__ bool next_seg(const Args& a, int64_t& u, int64_t u_en
   return true;
 }
 
-__device__ __forceinline__ void deq_bar_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kDeqWarps * 32) : "memory");
+// The data-parallel schedule's single segment: the whole tile of this CTA.
+__device__ __forceinline__ Seg tile_seg(const Args& a) {
+  Seg sg;
+  sg.tile = blockIdx.y * a.tiles_n + blockIdx.x;
+  sg.cb = 0;
+  sg.ce = a.n_chunks;
+  sg.n0 = blockIdx.x * kN;
+  sg.m0 = blockIdx.y * (kMT * kMaxTiles);
+  const int rows = (a.M - sg.m0 + kMT - 1) / kMT;
+  sg.tiles = rows < kMaxTiles ? rows : kMaxTiles;
+  return sg;
 }
 
-template <typename XT>
+// Segment `seg` of this CTA's work (kSK: the next part of its unit range;
+// otherwise its one tile), or false after the last.
+template <bool kSK>
+__device__ __forceinline__ bool get_seg(const Args& a, int64_t& u, int64_t u_end, int seg, Seg& sg) {
+  if constexpr (kSK) {
+    return next_seg(a, u, u_end, sg);
+  } else {
+    if (seg > 0) return false;
+    sg = tile_seg(a);
+    return true;
+  }
+}
+
+// kSK: the stream-K schedule; otherwise one tile per CTA (compiled without the
+// split-tile epilogue, which keeps the hot loops' register allocation lean).
+template <typename XT, bool kSK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                         const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
@@ -183,13 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nc = args.n_chunks;
   const Sched sched{(int64_t)args.n_tiles * nc, (int)gridDim.x};
-  int64_t u_begin, u_end;
-  if (args.stream_k) {
+  int64_t u_begin = 0, u_end = 0;
+  if constexpr (kSK) {
     u_begin = sched.bound(blockIdx.x);
     u_end = sched.bound(blockIdx.x + 1);
-  } else {
-    u_begin = (int64_t)(blockIdx.y * args.tiles_n + blockIdx.x) * nc;
-    u_end = u_begin + nc;
   }
 
   if (threadIdx.x == 0) {
@@ -226,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pdl_wait();
       int it = 0, issued = 0, seg = 0;
       Seg sg;
-      for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+      for (int64_t u = u_begin; !*abort_flag && get_seg<kSK>(args, u, u_end, seg, sg); ++seg) {
         // the previous segment's epilogue stages its tile in the ring
         if (seg > 0 && !mbar_wait_bounded(epi_done, (uint32_t)(seg - 1) & 1u, args.err, 1)) {
           *abort_flag = 1;
@@ -261,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0, seg = 0;
       Seg sg;
-      for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+      for (int64_t u = u_begin; !*abort_flag && get_seg<kSK>(args, u, u_end, seg, sg); ++seg) {
         // the previous segment's epilogue has read the accumulators
         if (seg > 0 && !mbar_wait_bounded(epi_done, (uint32_t)(seg - 1) & 1u, args.err, 2)) {
           *abort_flag = 1;
@@ -304,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stage = smem + warp * kEpiStage;
     int it = 0, seg = 0;
     Seg sg;
-    for (int64_t u = u_begin; !*abort_flag && next_seg(args, u, u_end, sg); ++seg) {
+    for (int64_t u = u_begin; !*abort_flag && get_seg<kSK>(args, u, u_end, seg, sg); ++seg) {
       for (int c = sg.cb; c < sg.ce; ++c, ++it) {
         const int slot = it % kStages;
         if (*abort_flag) break;
@@ -361,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Warp w owns a region of the tile: TMEM lanes 32 (w % 4) .. + 31 of each
       // row tile (a warp may only read its sub-partition's lane quarter) and
       // columns 128 (w / 4) .. + 127.
-      const bool whole = sg.cb == 0 && sg.ce == nc;
+      const bool whole = !kSK || (sg.cb == 0 && sg.ce == nc);
       int n_pieces = 1, first_cta = 0, end_slot = 1;
       float* own_part = nullptr;
       if (!whole) {
@@ -528,8 +550,8 @@ namespace {
 // epilogue (~10 chunks); stream-K costs an even share of all chunks plus up
 // to two partial epilogues and one output epilogue, plus the reads of the
 // other pieces of a split tile by the CTA that finishes it (a 256 KiB fp32
-// piece per ~14 chunk times, measured), and is taken when it saves 15% or
-// more.
+// piece per ~14 chunk times, measured). The grid with the lowest cost is
+// taken when it saves 15% or more.
 struct SkPlan {
   int grid;
   int64_t n_tiles;
@@ -555,14 +577,19 @@ SkPlan sk_plan(int64_t M, int64_t N, int64_t K) {
   // up to 128 rows the automatic regime runs the decode GEMV, not this kernel
   if (M <= 128 || nc <= 0 || sms <= 0 || p.n_tiles > kSkMaxTiles) return p;
   const int64_t total = p.n_tiles * nc;
-  int64_t grid = total / kMinChunksPerCta;
-  if (grid > sms) grid = sms;
-  if (grid < 2) return p;
-  const int64_t per_cta = cdiv(total, grid);
-  const int64_t pieces = per_cta >= nc ? 2 : cdiv(nc, per_cta) + 1;
   const int64_t dp = cdiv(p.n_tiles, sms) * (nc + kEpiChunks);
-  const int64_t sk = per_cta + 3 * kEpiChunks + kPieceReadChunks * (pieces - 1);
-  if (sk * 100 > dp * 85) return p;
+  int64_t best = dp, grid = 0;
+  const int64_t max_grid = total / kMinChunksPerCta < sms ? total / kMinChunksPerCta : sms;
+  for (int64_t g = 2; g <= max_grid; ++g) {
+    const int64_t per_cta = cdiv(total, g);
+    const int64_t pieces = per_cta >= nc ? 2 : cdiv(nc, per_cta) + 1;
+    const int64_t sk = per_cta + 3 * kEpiChunks + kPieceReadChunks * (pieces - 1);
+    if (sk < best) {
+      best = sk;
+      grid = g;
+    }
+  }
+  if (grid == 0 || best * 100 > dp * 85) return p;
   p.grid = (int)grid;
   p.bytes = kSkOff + (size_t)2 * grid * (kMT * kMaxTiles) * kN * sizeof(float) + kSkCounterBytes;
   return p;
@@ -583,12 +610,12 @@ extern "C" int tf_qlinear_gemm_stream_k_grid(int64_t M, int64_t N, int64_t K) {
 
 namespace tf {
 
-template <typename XT>
+template <typename XT, bool kSK>
 static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
   using namespace tc;
-  auto kern = gemm_int4_tc_kernel<XT>;
+  auto kern = gemm_int4_tc_kernel<XT, kSK>;
   const size_t smem = (size_t)kStages * kStage + 1024 + 128;
-  static bool attr_set[64] = {false};  // per element type and device
+  static bool attr_set[64] = {false};  // per instantiation and device
   const int dev = current_device() & 63;
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -653,8 +680,12 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
     a.counters = reinterpret_cast<int*>(ws + ((pb.workspace_bytes - kSkCounterBytes) & ~(size_t)15));
     grid = dim3((unsigned)plan.grid, 1);
   }
-  if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16>(grid, maps, a, st);
-  return launch_gemm<__half>(grid, maps, a, st);
+  if (a.stream_k) {
+    if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16, true>(grid, maps, a, st);
+    return launch_gemm<__half, true>(grid, maps, a, st);
+  }
+  if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16, false>(grid, maps, a, st);
+  return launch_gemm<__half, false>(grid, maps, a, st);
 }
 
 }  // namespace tf
