@@ -151,10 +151,13 @@ class _Workspaces:
     """Zero-initialised scratch handed to the kernels, one buffer per (device,
     stream). Its 256-byte header is shared by every kernel: word 0 is the device
     error word of their bounded waits (a wait that gives up after 1 s sets a
-    bit there and the launch still reports success). After the header only
-    tf_lm_head_argmax keeps anything: a counter it leaves zeroed and per-CTA
-    partial results. Calls that share a buffer are ordered on their stream.
-    ``errors`` reads the word of every buffer.
+    bit there and the launch still reports success). After the header,
+    tf_lm_head_argmax keeps a counter it leaves zeroed and per-CTA partial
+    results, and the prefill GEMM's stream-K schedule keeps partial tiles
+    (from byte 512) and arrival counters it leaves zeroed (the buffer's last
+    64 KiB); a buffer smaller than tf_qlinear_workspace_bytes runs the GEMM
+    one tile per CTA instead. Calls that share a buffer are ordered on their
+    stream. ``errors`` reads the word of every buffer.
 
     A buffer is zeroed only when it is (re)allocated. Reallocation happens
     outside any CUDA-graph capture: callers that capture size it first with
