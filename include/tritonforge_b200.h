@@ -194,6 +194,29 @@ int tf_rope_kv_append(const void* qkv, int64_t ld_qkv, void* q_out, const void* 
                       int64_t B, int32_t hq, int32_t hkv, int32_t head_dim, int64_t t_max, int dtype,
                       void* stream);
 
+/* ---- prompt prefill support ---------------------------------------------
+ * No reference counterpart as kernels: the reference's prefill runs through
+ * transformers (rotary embedding, DynamicCache, and `_mlp_forward`'s swiglu
+ * on separate gate/up outputs; reference integration/qwen.py:118-144).
+ *
+ * tf_rope_kv_prefill: t0 rows of the fused q|k|v projection [t0, (hq +
+ * 2*hkv) * D] (row stride ld_qkv elements) -> q_out rows [t0, hq * D] (row
+ * stride ld_q) rotated, in place when q_out == qkv and ld_q == ld_qkv; k
+ * rotated and v copied into positions 0..t0-1 of one sequence's caches
+ * [hkv, t_max, D]. cos/sin tables [>= t0, D] in the model dtype; rounding as
+ * tf_rope_kv_append. D a multiple of 16; pointers and rows 16-byte aligned.
+ */
+int tf_rope_kv_prefill(const void* qkv, int64_t ld_qkv, void* q_out, int64_t ld_q, const void* cos_table,
+                       const void* sin_table, void* k_cache, void* v_cache, int64_t t0, int32_t hq,
+                       int32_t hkv, int32_t head_dim, int64_t t_max, int dtype, void* stream);
+
+/* tf_swiglu_gu: act [M, inter] = silu(gate) * up from the fused gate|up
+ * projection [M, 2*inter] (row stride ld_gu) whose columns interleave gate
+ * and up per 64 (gate j at 128 (j / 64) + j % 64, up 64 further); rounding
+ * as tf_swiglu. inter a multiple of 64; pointers and rows 16-byte aligned. */
+int tf_swiglu_gu(const void* gu, int64_t ld_gu, void* act, int64_t ld_act, int64_t M, int64_t inter,
+                 int dtype, void* stream);
+
 /* tf_decode_attention: out [B, hq, D] = softmax(q k^T * scale) v over the
  * first *len (device int) cached positions; grouped-query (hq % hkv == 0),
  * D in {64, 128}; fp32 scores/softmax/accumulation, one rounding. */

@@ -65,3 +65,67 @@ def test_prefill_needs_k_major_projections():
     d = QwenDecoder(w, 16, 64)  # batches 9..64: column-major projections
     with pytest.raises(RuntimeError, match="K-major"):
         d.prefill_tokens(torch.zeros(16, 8, dtype=torch.long))
+
+
+def _rope_ref(t: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    # transformers' apply_rotary_pos_emb in the model dtype: each product and the sum rounded
+    h = t.shape[-1] // 2
+    return t * cos + torch.cat((-t[..., h:], t[..., :h]), dim=-1) * sin
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("t0,hq,hkv,d", [(37, 28, 4, 128), (200, 14, 2, 64), (1, 8, 8, 128)])
+@pytest.mark.parametrize("in_place", [True, False])
+def test_rope_kv_prefill_bit_exact(t0, hq, hkv, d, dtype, in_place):
+    """tf_rope_kv_prefill against transformers' rounding in torch: q (in place
+    over the projection, or into another buffer), k and v in the cache, bit
+    for bit; cache positions past the prompt untouched."""
+    from tritonforge_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(t0 + hq)
+    width = (hq + 2 * hkv) * d
+    ld = width + 16
+    qkv = torch.randn(t0, ld, generator=g).to(dtype).to(dev)
+    t_max = t0 + 5
+    ang = torch.rand(t_max, d // 2, generator=g) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(dtype).to(dev)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(dtype).to(dev)
+    kc = torch.full((hkv, t_max, d), float("nan"), dtype=dtype, device=dev)
+    vc = torch.full_like(kc, float("nan"))
+    c, s = cos[:t0, None, :], sin[:t0, None, :]
+    want_q = _rope_ref(qkv[:, :hq * d].view(t0, hq, d), c, s)
+    want_k = _rope_ref(qkv[:, hq * d:(hq + hkv) * d].view(t0, hkv, d), c, s).transpose(0, 1)
+    want_v = qkv[:, (hq + hkv) * d:width].view(t0, hkv, d).transpose(0, 1).clone()
+    before = qkv.clone()
+    q_out = qkv if in_place else torch.zeros(t0, hq * d + 8, dtype=dtype, device=dev)
+    _lib.check(_lib.load().tf_rope_kv_prefill(qkv.data_ptr(), ld, q_out.data_ptr(), q_out.stride(0), cos.data_ptr(),
+                                              sin.data_ptr(), kc.data_ptr(), vc.data_ptr(), t0, hq, hkv, d, t_max,
+                                              _lib.dtype_code(dtype), _lib.stream_ptr(dev)), "rope_kv_prefill")
+    torch.cuda.synchronize()
+    assert torch.equal(q_out[:, :hq * d].view(t0, hq, d), want_q)
+    assert torch.equal(kc[:, :t0], want_k) and torch.equal(vc[:, :t0], want_v)
+    assert torch.isnan(kc[:, t0:].float()).all() and torch.isnan(vc[:, t0:].float()).all()
+    assert torch.equal(qkv[:, hq * d:], before[:, hq * d:]), "k, v columns and padding are read only"
+    if not in_place:
+        assert torch.equal(qkv, before)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("m,inter", [(1, 64), (37, 4864), (2048, 18944)])
+def test_swiglu_gu_matches_swiglu_on_the_halves(m, inter, dtype):
+    """tf_swiglu_gu on the per-64 interleaved gate|up output equals tf_swiglu on
+    the de-interleaved halves bit for bit (and so the oracle's rounding)."""
+    from tritonforge_b200 import _lib, kernels
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(m + inter)
+    gu = (torch.randn(m, 2 * inter + 32, generator=g) * 3).to(dtype).to(dev)
+    v = gu[:, :2 * inter].view(m, inter // 64, 2, 64)
+    want = kernels.swiglu(v[:, :, 0].contiguous(), v[:, :, 1].contiguous()).view(m, inter)
+    act = torch.full((m, inter + 8), float("nan"), dtype=dtype, device=dev)
+    _lib.check(_lib.load().tf_swiglu_gu(gu.data_ptr(), gu.stride(0), act.data_ptr(), act.stride(0), m, inter,
+                                        _lib.dtype_code(dtype), _lib.stream_ptr(dev)), "swiglu_gu")
+    torch.cuda.synchronize()
+    assert torch.equal(act[:, :inter], want)
+    assert torch.isnan(act[:, inter:].float()).all()

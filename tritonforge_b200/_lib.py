@@ -39,6 +39,9 @@ SIGNATURES = {
     "tf_last_error_message": (ctypes.c_char_p, []),
     "tf_qlinear_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
     "tf_qlinear_gemm_stream_k_grid": (_i32, [_i64, _i64, _i64]),
+    "tf_rope_kv_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32,
+                                  _vp]),
+    "tf_swiglu_gu": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _vp]),
     "tf_qlinear": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,
                           _i64, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
     "tf_qlinear_ex": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64,

@@ -706,12 +706,13 @@ class QwenDecoder:
         norms, every projection through quantized_linear (the tcgen05 GEMM for
         more than 128 rows; under tensor parallelism the row-parallel fp32
         partials are all-reduced and rounded once), RoPE with transformers'
-        roundings, causal attention over the prompt (the library's
-        scaled-dot-product attention: the prompt's keys and values are written
-        to the static cache first), and the lm_head + argmax of the last
-        positions. Sets the first generated tokens and the position; needs the
-        reference's K-major projections (QuantLinear; the column-major layout
-        serves up to 64 rows)."""
+        roundings (q rotated in place, keys and values written to the static
+        cache: tf_rope_kv_prefill), causal attention over the prompt (the
+        library's scaled-dot-product attention over the cache), SwiGLU straight
+        from the interleaved gate|up output (tf_swiglu_gu), and the lm_head +
+        argmax of the last positions. Sets the first generated tokens and the
+        position; needs the reference's K-major projections (QuantLinear; the
+        column-major layout serves up to 64 rows)."""
         import torch.nn.functional as F
 
         if prompt.shape[0] != self.B:
@@ -734,12 +735,7 @@ class QwenDecoder:
         qkv, o, gu, act = buf(t0, hq + 2 * hkv), buf(t0, H), buf(t0, 2 * self.I), buf(t0, self.I)
         part = buf(t0, H, dtype=torch.float32) if self.tp else None
         last = buf(self.B, H)
-        cos, sin = self.cos[:t0, None, :], self.sin[:t0, None, :]
-
-        def rope(t: torch.Tensor) -> torch.Tensor:
-            # [T0, heads, D]: (t * cos) + (rotate_half(t) * sin), each product and the sum rounded
-            h = D // 2
-            return t * cos + torch.cat((-t[..., h:], t[..., :h]), dim=-1) * sin
+        code = _lib.dtype_code(dt)
 
         def row_parallel(xin, ql, weight, res, res_next):
             if self.tp:
@@ -760,20 +756,20 @@ class QwenDecoder:
             kernels.rmsnorm(x, self.layers[0]["in_norm"], self.eps, out=normed)
             for li, L in enumerate(self.layers):
                 self._lin(normed, L["qkv"], qkv)
-                q = rope(qkv[:, :hq].view(t0, self.Hq, D))
-                k = rope(qkv[:, hq:hq + hkv].view(t0, self.Hkv, D))
-                v = qkv[:, hq + hkv:].view(t0, self.Hkv, D)
-                self.k_cache[li, b, :, :t0].copy_(k.transpose(0, 1))
-                self.v_cache[li, b, :, :t0].copy_(v.transpose(0, 1))
-                a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], self.k_cache[li, b:b + 1, :, :t0],
-                                                   self.v_cache[li, b:b + 1, :, :t0], is_causal=True,
+                kc, vc = self.k_cache[li, b], self.v_cache[li, b]
+                _lib.check(lib.tf_rope_kv_prefill(qkv.data_ptr(), qkv.stride(0), qkv.data_ptr(), qkv.stride(0),
+                                                  self.cos.data_ptr(), self.sin.data_ptr(), kc.data_ptr(),
+                                                  vc.data_ptr(), t0, self.Hq, self.Hkv, D, self.T, code, st),
+                           "rope_kv_prefill")
+                q = qkv[:, :hq].view(t0, self.Hq, D).transpose(0, 1)[None]
+                a = F.scaled_dot_product_attention(q, kc[None, :, :t0], vc[None, :, :t0], is_causal=True,
                                                    scale=self.scale, enable_gqa=True)
                 attn = a[0].transpose(0, 1).reshape(t0, hq)
                 row_parallel(attn, L["o"], L["post_norm"], res, res_next)
                 res, res_next = res_next, res
                 self._lin(normed, L["gu"], gu)
-                g4 = gu.view(t0, -1, 2, 64)
-                kernels.swiglu(g4[:, :, 0], g4[:, :, 1], out=act.view(t0, -1, 64))
+                _lib.check(lib.tf_swiglu_gu(gu.data_ptr(), gu.stride(0), act.data_ptr(), act.stride(0), t0, self.I,
+                                            code, st), "swiglu_gu")
                 nxt = self.layers[li + 1]["in_norm"] if li + 1 < nl else self.final_norm
                 row_parallel(act, L["down"], nxt, res, res_next)
                 res, res_next = res_next, res
