@@ -239,12 +239,14 @@ int tf_swiglu_strided(const void* gate, const void* up, void* out, int64_t M, in
                       int64_t ldu, int64_t ldo, int dtype, void* stream);
 
 /* tf_qlinear_swiglu: the gate and up projections of a SwiGLU MLP in one
- * decode-regime int4 linear (no reference counterpart: the reference runs
- * quantized_linear twice and then swiglu, integration/qwen.py:118-121). The
- * N = 2 I weight columns are interleaved per 128-column block as [gate 64 |
- * up 64]; out [M, I] (row stride ldo) = round(silu(g) * u) with
- * g = round(x @ Wg), u = round(x @ Wu) in x's dtype (no bias). M <= 32 and the
- * decode regime's other constraints, N % 128 == 0. Workspace as tf_qlinear. */
+ * int4 linear (no reference counterpart: the reference runs quantized_linear
+ * twice and then swiglu, integration/qwen.py:118-121). The N = 2 I weight
+ * columns are interleaved per 128-column block as [gate 64 | up 64]; out
+ * [M, I] (row stride ldo) = round(silu(g) * u) with g = round(x @ Wg),
+ * u = round(x @ Wu) in x's dtype (no bias). The regimes of tf_qlinear: the
+ * decode GEMV up to 32 rows, 32-row chunks of it up to 128, above that the
+ * tcgen05 GEMM with the SwiGLU in its epilogue (the [M, N] projection is
+ * never written). N % 128 == 0. Workspace as tf_qlinear. */
 int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
                       const void* zeros, int param_dtype, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
                       int64_t K_pad, int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);

@@ -335,8 +335,13 @@ def test_auto_regime_between_33_and_128_rows(m, n, k, dtype):
 # ---- fused gate|up + SwiGLU (decode regime) --------------------------------
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("m,i,k", [(1, 4864, 896), (8, 4864, 896), (3, 896, 4864), (16, 18944, 3584),
-                                   (32, 7424, 8192), (5, 1024, 29568)])
+                                   (32, 7424, 8192), (5, 1024, 29568), (40, 4864, 896), (200, 4864, 896),
+                                   (300, 1024, 16384), (1100, 896, 4864)])
 def test_qlinear_swiglu(m, i, k, dtype):
+    """The fused gate|up + SwiGLU in every regime: the decode GEMV (M <= 32),
+    its 32-row chunks (40), the GEMM's SwiGLU epilogue one tile per CTA (200,
+    1100) and on the stream-K schedule (300 x 1024 x 16384), against the
+    oracle's separately rounded projections."""
     from tritonforge_b200.tp import interleave_gate_up
 
     g = torch.Generator().manual_seed(m + i)
@@ -349,7 +354,9 @@ def test_qlinear_swiglu(m, i, k, dtype):
     scales = interleave_gate_up(sg, su).contiguous()
     zeros = interleave_gate_up(zg, zu).contiguous()
     out = torch.full((m, i), float("nan"), dtype=dtype, device="cuda")
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    need = _lib.load().tf_qlinear_workspace_bytes(m, 2 * i, packed.shape[0] * 2, GROUP)
+    assert (m, i, k) != (300, 1024, 16384) or _lib.load().tf_qlinear_gemm_stream_k_grid(m, 2 * i, k) > 0
+    ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device="cuda")
     rc = _lib.load().tf_qlinear_swiglu(x.data_ptr(), x.stride(0), _lib.dtype_code(dtype), packed.data_ptr(),
                                        scales.data_ptr(), zeros.data_ptr(), _lib.dtype_code(dtype), out.data_ptr(),
                                        out.stride(0), m, 2 * i, k, packed.shape[0] * 2, GROUP, ws.data_ptr(),
@@ -358,3 +365,4 @@ def test_qlinear_swiglu(m, i, k, dtype):
     gate = oracle_linear(x, pg, sg, zg, None)  # the separate projections, rounded to the dtype
     up = oracle_linear(x, pu, su, zu, None)
     assert_swiglu_close(out, gate, up, dtype, f"qlinear_swiglu {m}x{i}x{k}")
+    assert int(ws[:4].view(torch.int32).item()) == 0

@@ -41,14 +41,14 @@ int validate(const QLinearProblem& pb) {
 constexpr int64_t kGemvChunkMaxM = 128;
 constexpr int64_t kGemvChunkRows = 32;
 
-int gemv_chunks_launch(const QLinearProblem& pb, cudaStream_t st) {
+int gemv_chunks_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = false) {
   const int64_t osz = pb.out_f32 ? 4 : 2;  // out is fp32 or x's 16-bit type
   for (int64_t r = 0; r < pb.M; r += kGemvChunkRows) {
     QLinearProblem c = pb;
     c.M = pb.M - r < kGemvChunkRows ? pb.M - r : kGemvChunkRows;
     c.x = static_cast<const uint8_t*>(pb.x) + r * pb.ldx * 2;
     c.out = static_cast<uint8_t*>(pb.out) + r * pb.ldo * osz;
-    const int rc = gemv_launch(c, st);
+    const int rc = gemv_launch(c, st, swiglu);
     if (rc != TF_OK) return rc;
   }
   return TF_OK;
@@ -135,8 +135,16 @@ extern "C" int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const 
   if (M == 0 || N == 0) return TF_OK;
   pb.ldo = ldo;
   if (N % 128 != 0) return fail(TF_ERR_BAD_SHAPE, "qlinear_swiglu: N=%lld not a multiple of 128", (long long)N);
-  if (!gemv_supported(pb)) return fail(TF_ERR_UNSUPPORTED, "qlinear_swiglu: needs the decode regime (M <= 32)");
-  return gemv_launch(pb, static_cast<cudaStream_t>(stream), true);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the regimes of tf_qlinear: the decode GEMV, its 32-row chunks, the GEMM
+  if (gemv_supported(pb)) return gemv_launch(pb, st, true);
+  if (pb.M <= kGemvChunkMaxM) {
+    QLinearProblem c = pb;
+    c.M = kGemvChunkRows;
+    if (gemv_supported(c)) return gemv_chunks_launch(pb, st, true);
+  }
+  if (gemm_supported(pb)) return gemm_launch(pb, st, true);
+  return fail(TF_ERR_UNSUPPORTED, "qlinear_swiglu: no regime takes this problem (alignment or dtypes)");
 }
 
 extern "C" size_t tf_qlinear_cm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad) {

@@ -49,7 +49,8 @@ int gemv_cm_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = fals
 
 bool gemm_supported(const QLinearProblem& pb);
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad);
-int gemm_launch(const QLinearProblem& pb, cudaStream_t st);
+// swiglu: out [M, N/2] = silu(gate) * up of the per-64 interleaved gate|up columns
+int gemm_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu = false);
 
 int simt_launch(const QLinearProblem& pb, cudaStream_t st);
 

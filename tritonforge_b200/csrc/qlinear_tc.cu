@@ -71,6 +71,8 @@ struct Args {
   int bias_dtype;
   uint32_t idesc;      // tcgen05 instruction descriptor
   int out_f32;         // store the fp32 sums unrounded (a row-parallel partial, no bias)
+  int swiglu;          // out [M, N/2] = silu(gate) * up of the per-64 interleaved gate|up columns (no bias;
+                       // the kSwiGLU build)
   // Schedule. Tiles of 256 columns x 256 rows, column-fastest; a unit is one
   // 64-k chunk of one tile. Data-parallel (stream_k = 0, the kernel built
   // without kSK): the grid is (column tiles, row groups) and each CTA runs
@@ -188,7 +190,8 @@ __device__ __forceinline__ bool get_seg(const Args& a, int64_t& u, int64_t u_end
 
 // kSK: the stream-K schedule; otherwise one tile per CTA (compiled without the
 // split-tile epilogue, which keeps the hot loops' register allocation lean).
-template <typename XT, bool kSK>
+// kSwiGLU: the SwiGLU epilogue (Args::swiglu), a build of its own likewise.
+template <typename XT, bool kSK, bool kSwiGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                         const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
@@ -433,7 +436,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this warp's 16 KiB of the idle ring as boxes of [32 rows x 128 bytes]
       // in the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8):
       // conflict-free for row-per-lane writes) and stored by one lane with TMA
-      // (rows and columns outside the output are not written).
+      // (rows and columns outside the output are not written). With the SwiGLU
+      // epilogue the warp's 128 columns are one [gate 64 | up 64] block of the
+      // interleaved projection and become 64 outputs, one box.
+      auto fetch = [&](int t, int row, int cc, uint32_t (&r)[32]) {
+        if (whole) {
+          tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
+          return;
+        }
+        // every piece from the partial slots (this CTA's own included), in k order
+        float acc[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+#pragma unroll 1
+        for (int p = 0; p < n_pieces; ++p) {
+          const int g = first_cta + p;
+          const float4* part = reinterpret_cast<const float4*>(
+              args.partials + (size_t)(2 * g + (p == n_pieces - 1 ? end_slot : 1)) * (kMT * kMaxTiles * kN)) +
+              (size_t)(cc / 4) * (kMT * kMaxTiles) + row;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 f = __ldcg(part + q * (kMT * kMaxTiles));
+            acc[4 * q] += f.x;
+            acc[4 * q + 1] += f.y;
+            acc[4 * q + 2] += f.z;
+            acc[4 * q + 3] += f.w;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(acc[e]);
+      };
       const int box_cols = args.out_f32 ? 32 : 64;  // columns per 128-byte box row
       for (int t = 0; t < sg.tiles; ++t) {
         if (t > 0) {  // the previous tile's stores have read the staging area
@@ -441,60 +473,64 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
         const int row = t * kMT + 32 * quad + lane;
-        for (int lc = 0; lc < kN / 2; lc += 32) {
-          const int cc = c_base + lc;
-          uint32_t r[32];
-          if (whole) {
-            tmem_ld32(tmem + ((uint32_t)(32 * quad) << 16) + t * kN + cc, r);
-          } else {
-            // every piece from the partial slots (this CTA's own included), in k order
-            float acc[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-#pragma unroll 1
-            for (int p = 0; p < n_pieces; ++p) {
-              const int g = first_cta + p;
-              const float4* part = reinterpret_cast<const float4*>(
-                  args.partials + (size_t)(2 * g + (p == n_pieces - 1 ? end_slot : 1)) * (kMT * kMaxTiles * kN)) +
-                  (size_t)(cc / 4) * (kMT * kMaxTiles) + row;
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 f = __ldcg(part + q * (kMT * kMaxTiles));
-                acc[4 * q] += f.x;
-                acc[4 * q + 1] += f.y;
-                acc[4 * q + 2] += f.z;
-                acc[4 * q + 3] += f.w;
-              }
-            }
-#pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(acc[e]);
-          }
-          if (args.out_f32) {
-            uint8_t* srow = stage + (lc / 32) * 4096 + lane * 128;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4*>(srow + (((uint32_t)q ^ rsw) << 4)) =
-                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-          } else {
-            uint32_t h[16];
+        if constexpr (kSwiGLU) {
+          for (int lc = 0; lc < 64; lc += 32) {
+            uint32_t gr[32], ur[32], h[16];
+            fetch(t, row, c_base + lc, gr);
+            fetch(t, row, c_base + 64 + lc, ur);
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
-              if (args.bias) {
-                const int col = sg.n0 + cc + e;
-                if (col < args.N) v0 += load_as_f32(args.bias, col, args.bias_dtype);
-                if (col + 1 < args.N) v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
+              // g = round(x Wg), u = round(x Wu), out = round(silu(g) * u) (swiglu.py:21-30)
+              float o[2];
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const float gv = round_to<XT>(__uint_as_float(gr[e + i]));
+                const float uv = round_to<XT>(__uint_as_float(ur[e + i]));
+                const float sig = 1.0f / (1.0f + expf(-gv));
+                o[i] = (gv * sig) * uv;
               }
-              const XT a = Num<XT>::from_f(v0), b = Num<XT>::from_f(v1);
+              const XT a = Num<XT>::from_f(o[0]), b = Num<XT>::from_f(o[1]);
               h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
                          ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
             }
-            uint8_t* srow = stage + (lc / 64) * 4096 + lane * 128;
-            const int c0 = (lc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
+            uint8_t* srow = stage + lane * 128;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(srow + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
+              *reinterpret_cast<uint4*>(srow + (((uint32_t)(lc / 8 + q) ^ rsw) << 4)) =
                   make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+          }
+        } else {
+          for (int lc = 0; lc < kN / 2; lc += 32) {
+            const int cc = c_base + lc;
+            uint32_t r[32];
+            fetch(t, row, cc, r);
+            if (args.out_f32) {
+              uint8_t* srow = stage + (lc / 32) * 4096 + lane * 128;
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<uint4*>(srow + (((uint32_t)q ^ rsw) << 4)) =
+                    make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            } else {
+              uint32_t h[16];
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
+                if (args.bias) {
+                  const int col = sg.n0 + cc + e;
+                  if (col < args.N) v0 += load_as_f32(args.bias, col, args.bias_dtype);
+                  if (col + 1 < args.N) v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
+                }
+                const XT a = Num<XT>::from_f(v0), b = Num<XT>::from_f(v1);
+                h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
+                           ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
+              }
+              uint8_t* srow = stage + (lc / 64) * 4096 + lane * 128;
+              const int c0 = (lc % 64) / 8;  // first 16-byte chunk of these 32 columns in the box row
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(srow + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
+                    make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+            }
           }
         }
         // the generic-proxy writes become visible to the TMA unit, then one lane stores
@@ -502,8 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           const int row0 = sg.m0 + t * kMT + 32 * quad;
-          for (int b = 0; b < (kN / 2) / box_cols; ++b)
-            tma_store_2d(&omap, stage + b * 4096, sg.n0 + c_base + b * box_cols, row0);
+          if constexpr (kSwiGLU) {
+            tma_store_2d(&omap, stage, (sg.n0 + c_base) / 2, row0);
+          } else {
+            for (int b = 0; b < (kN / 2) / box_cols; ++b)
+              tma_store_2d(&omap, stage + b * 4096, sg.n0 + c_base + b * box_cols, row0);
+          }
           bulk_commit_group();
         }
       }
@@ -610,10 +650,10 @@ extern "C" int tf_qlinear_gemm_stream_k_grid(int64_t M, int64_t N, int64_t K) {
 
 namespace tf {
 
-template <typename XT, bool kSK>
+template <typename XT, bool kSK, bool kSwiGLU>
 static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
   using namespace tc;
-  auto kern = gemm_int4_tc_kernel<XT, kSK>;
+  auto kern = gemm_int4_tc_kernel<XT, kSK, kSwiGLU>;
   const size_t smem = (size_t)kStages * kStage + 1024 + 128;
   static bool attr_set[64] = {false};  // per instantiation and device
   const int dev = current_device() & 63;
@@ -626,7 +666,7 @@ static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cu
                    maps[3], maps[4], a);
 }
 
-int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
+int gemm_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu) {
   using namespace tc;
   if (!pb.workspace || pb.workspace_bytes < kWsHeader)
     return fail(TF_ERR_WORKSPACE, "qlinear(gemm): workspace %zu bytes < required %zu", pb.workspace_bytes,
@@ -647,11 +687,14 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   rc = encode_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.zeros, (uint64_t)pb.N, (uint64_t)groups,
                             (uint64_t)pb.N * 2, kN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  // out [M rows, N] in boxes of 32 rows x 128 bytes (64 halves or 32 floats), 128-byte swizzle
+  // out [M rows, N] (with the SwiGLU epilogue [M, N/2]) in boxes of 32 rows x
+  // 128 bytes (64 halves or 32 floats), 128-byte swizzle
   const bool f32 = pb.out_f32 != 0;
+  if (swiglu && (f32 || pb.bias || pb.N % 128))
+    return fail(TF_ERR_UNSUPPORTED, "qlinear(gemm): the SwiGLU epilogue takes 16-bit output, no bias, N %% 128 == 0");
   rc = encode_tensor_map_2d(&maps[4], f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.out,
-                            (uint64_t)pb.N, (uint64_t)pb.M, (uint64_t)pb.ldo * (f32 ? 4 : 2), f32 ? 32 : 64, 32,
-                            CU_TENSOR_MAP_SWIZZLE_128B);
+                            (uint64_t)(swiglu ? pb.N / 2 : pb.N), (uint64_t)pb.M, (uint64_t)pb.ldo * (f32 ? 4 : 2),
+                            f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   Args a{};
   a.bias = pb.bias;
@@ -659,6 +702,7 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
   a.out = pb.out;
   a.ldo = pb.ldo;
   a.out_f32 = pb.out_f32;
+  a.swiglu = swiglu ? 1 : 0;
   a.err = reinterpret_cast<int*>(pb.workspace);
   a.M = (int)pb.M;
   a.N = (int)pb.N;
@@ -680,12 +724,17 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st) {
     a.counters = reinterpret_cast<int*>(ws + ((pb.workspace_bytes - kSkCounterBytes) & ~(size_t)15));
     grid = dim3((unsigned)plan.grid, 1);
   }
+  const bool bf16 = pb.x_dtype == TF_BF16;
   if (a.stream_k) {
-    if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16, true>(grid, maps, a, st);
-    return launch_gemm<__half, true>(grid, maps, a, st);
+    if (swiglu) return bf16 ? launch_gemm<__nv_bfloat16, true, true>(grid, maps, a, st)
+                            : launch_gemm<__half, true, true>(grid, maps, a, st);
+    return bf16 ? launch_gemm<__nv_bfloat16, true, false>(grid, maps, a, st)
+                : launch_gemm<__half, true, false>(grid, maps, a, st);
   }
-  if (pb.x_dtype == TF_BF16) return launch_gemm<__nv_bfloat16, false>(grid, maps, a, st);
-  return launch_gemm<__half, false>(grid, maps, a, st);
+  if (swiglu) return bf16 ? launch_gemm<__nv_bfloat16, false, true>(grid, maps, a, st)
+                          : launch_gemm<__half, false, true>(grid, maps, a, st);
+  return bf16 ? launch_gemm<__nv_bfloat16, false, false>(grid, maps, a, st)
+              : launch_gemm<__half, false, false>(grid, maps, a, st);
 }
 
 }  // namespace tf

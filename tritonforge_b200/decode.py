@@ -607,32 +607,38 @@ class QwenDecoder:
                                               _lib.stream_ptr(self.dev)), "best_of_ranks")
 
     def _gate_up(self, x: torch.Tensor, ql, act: torch.Tensor) -> None:
-        """act = silu(x @ Wg) * (x @ Wu): one fused decode kernel for up to 32
-        rows (tf_qlinear_swiglu; up to 64 with column-major weights,
-        tf_qlinear_cm_swiglu), else the projection and a SwiGLU launch."""
+        """act = silu(x @ Wg) * (x @ Wu) in one int4 linear with the SwiGLU
+        fused: tf_qlinear_swiglu on K-major weights (any rows: decode GEMV,
+        its 32-row chunks, or the GEMM with a SwiGLU epilogue),
+        tf_qlinear_cm_swiglu on column-major weights (up to 64 rows)."""
         m, k = x.shape
         if isinstance(ql, CMLinear) and m <= 64:
             qlinear_cm_swiglu(x, ql.tiles, ql.scales, ql.zeros, ql.group_size, out=act)
             return
-        if isinstance(ql, QuantLinear) and m <= 32:
-            ws = _lib.workspaces.get(self.dev, 256)
+        if isinstance(ql, QuantLinear):
+            n, kp = ql.packed.shape[1], ql.packed.shape[0] * 2
+            ws = _lib.workspaces.get(self.dev, self._lib.tf_qlinear_workspace_bytes(m, n, kp, ql.group_size))
             _lib.check(self._lib.tf_qlinear_swiglu(
                 x.data_ptr(), x.stride(0), self._dt, ql.packed.data_ptr(), ql.scales.data_ptr(), ql.zeros.data_ptr(),
-                _lib.dtype_code(ql.scales.dtype), act.data_ptr(), act.stride(0), m, ql.packed.shape[1], k,
-                ql.packed.shape[0] * 2, ql.group_size, ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)),
-                "qlinear_swiglu")
+                _lib.dtype_code(ql.scales.dtype), act.data_ptr(), act.stride(0), m, n, k, kp, ql.group_size,
+                ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)), "qlinear_swiglu")
             return
         gu = self._lin(x, ql, self.buf["gu"]).view(m, -1, 2, 64)
         kernels.swiglu(gu[:, :, 0], gu[:, :, 1], out=act.view(m, -1, 64))
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step: the embedding gather,
-        the first RMSNorm, 7 or 8 per layer, the lm_head + argmax and, under
+        the first RMSNorm, per layer the four projections (gate|up with its
+        SwiGLU fused; K-major projections of 33..128 rows run as 32-row chunks,
+        one launch each), attention and the two residual + norm (or fused
+        all-reduce) launches, then the lm_head + argmax and, under
         vocabulary-parallel tensor parallelism, best_of_ranks."""
         n = 3 + (1 if self.vocab_parallel else 0)
         for L in self.layers:
-            fused = self.B <= (64 if isinstance(L["gu"], CMLinear) else 32)
-            n += 7 if fused else 8
+            n += 3
+            for name in ("qkv", "o", "gu", "down"):
+                chunked = not isinstance(L[name], CMLinear) and 32 < self.B <= 128
+                n += -(-self.B // 32) if chunked else 1
         return n
 
     @torch.no_grad()
@@ -708,8 +714,8 @@ class QwenDecoder:
         partials are all-reduced and rounded once), RoPE with transformers'
         roundings (q rotated in place, keys and values written to the static
         cache: tf_rope_kv_prefill), causal attention over the prompt (the
-        library's scaled-dot-product attention over the cache), SwiGLU straight
-        from the interleaved gate|up output (tf_swiglu_gu), and the lm_head +
+        library's scaled-dot-product attention over the cache), the gate|up
+        projection with SwiGLU in its epilogue (tf_qlinear_swiglu), and the lm_head +
         argmax of the last positions. Sets the first generated tokens and the
         position; needs the reference's K-major projections (QuantLinear; the
         column-major layout serves up to 64 rows)."""
@@ -732,7 +738,7 @@ class QwenDecoder:
             return torch.empty(*shape, dtype=dtype, device=dev)
 
         x, res_a, res_b, normed = buf(t0, H), buf(t0, H), buf(t0, H), buf(t0, H)
-        qkv, o, gu, act = buf(t0, hq + 2 * hkv), buf(t0, H), buf(t0, 2 * self.I), buf(t0, self.I)
+        qkv, o, act = buf(t0, hq + 2 * hkv), buf(t0, H), buf(t0, self.I)
         part = buf(t0, H, dtype=torch.float32) if self.tp else None
         last = buf(self.B, H)
         code = _lib.dtype_code(dt)
@@ -767,9 +773,7 @@ class QwenDecoder:
                 attn = a[0].transpose(0, 1).reshape(t0, hq)
                 row_parallel(attn, L["o"], L["post_norm"], res, res_next)
                 res, res_next = res_next, res
-                self._lin(normed, L["gu"], gu)
-                _lib.check(lib.tf_swiglu_gu(gu.data_ptr(), gu.stride(0), act.data_ptr(), act.stride(0), t0, self.I,
-                                            code, st), "swiglu_gu")
+                self._gate_up(normed, L["gu"], act)  # gate|up GEMM with SwiGLU in its epilogue
                 nxt = self.layers[li + 1]["in_norm"] if li + 1 < nl else self.final_norm
                 row_parallel(act, L["down"], nxt, res, res_next)
                 res, res_next = res_next, res
