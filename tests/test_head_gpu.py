@@ -121,3 +121,26 @@ def test_lm_head_vocab_slices_and_best_of_ranks():
                "best_of_ranks")
     torch.cuda.synchronize()
     assert torch.equal(tokens, torch.argmax(full, dim=-1))
+
+
+def test_engine_head_above_64_rows():
+    """A decode step at batch 100 runs the lm_head + argmax as two launches
+    (64 + 36 rows): every row's logits against torch's fp32 product of the
+    step's final normed rows, every token a maximum of its row, and the
+    position advanced once."""
+    from tritonforge_b200.decode import QwenDecoder, QwenWeights
+
+    dev = torch.device("cuda", 0)
+    w = QwenWeights.synthetic("7b", dtype=torch.bfloat16, device=dev, seed=5, layers=1)
+    d = QwenDecoder(w, 100, 32, colmajor=False)
+    d.fill_cache(8, seed=2)
+    pos0 = d.pos.clone()
+    d.step()
+    torch.cuda.synchronize()
+    assert (d.pos - pos0).tolist() == [1, 1]
+    logits = d.buf["logits"].float()
+    want = d.buf["normed"].float() @ w.lm_head.float().T
+    rms = float(want.pow(2).mean().sqrt())
+    assert float((logits - want).abs().max()) <= 2e-2 * rms
+    assert torch.equal(logits.gather(1, d.tokens[:, None])[:, 0], logits.max(-1).values)
+    assert d.device_errors() == 0

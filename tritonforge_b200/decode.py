@@ -498,6 +498,7 @@ class QwenDecoder:
         dist.all_reduce(t, group=self.group)
 
     STEP_PARTS = ("gemv", "attention", "reduce", "head")
+    HEAD_ROWS = 64  # rows per tf_lm_head_argmax launch
 
     @torch.no_grad()
     def step(self) -> torch.Tensor:
@@ -553,13 +554,19 @@ class QwenDecoder:
         winner) and pos += 1, in one kernel."""
         b = self.buf
         vp = self.vocab_parallel
-        ws = _lib.workspaces.get(self.dev, self._lib.tf_lm_head_workspace_bytes(self.B))
-        _lib.check(self._lib.tf_lm_head_argmax(
-            x.data_ptr(), x.stride(0), self.lm_head.data_ptr(), self.lm_head.stride(0),
-            self.lm_head.shape[0], self.lm_head.shape[1], self.B, _lib.dtype_code(self.lm_head.dtype),
-            b["logits"].data_ptr(), b["logits"].stride(0), None if vp else self.tokens.data_ptr(),
-            b["best"].data_ptr() if vp else None, self.v0 if vp else 0, self.pos.data_ptr(), self.pos.numel(),
-            ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)), "lm_head_argmax")
+        rows = self.HEAD_ROWS
+        ws = _lib.workspaces.get(self.dev, self._lib.tf_lm_head_workspace_bytes(min(self.B, rows)))
+        for r0 in range(0, self.B, rows):
+            # up to 64 rows per launch; the last launch advances the position
+            n = min(rows, self.B - r0)
+            last = r0 + n == self.B
+            _lib.check(self._lib.tf_lm_head_argmax(
+                x[r0:].data_ptr(), x.stride(0), self.lm_head.data_ptr(), self.lm_head.stride(0),
+                self.lm_head.shape[0], self.lm_head.shape[1], n, _lib.dtype_code(self.lm_head.dtype),
+                b["logits"][r0:].data_ptr(), b["logits"].stride(0), None if vp else self.tokens[r0:].data_ptr(),
+                b["best"][r0:].data_ptr() if vp else None, self.v0 if vp else 0,
+                self.pos.data_ptr() if last else None, self.pos.numel() if last else 0,
+                ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)), "lm_head_argmax")
         if vp:
             self._vocab_parallel_argmax()
 
@@ -633,7 +640,7 @@ class QwenDecoder:
         one launch each), attention and the two residual + norm (or fused
         all-reduce) launches, then the lm_head + argmax and, under
         vocabulary-parallel tensor parallelism, best_of_ranks."""
-        n = 3 + (1 if self.vocab_parallel else 0)
+        n = 2 + -(-self.B // self.HEAD_ROWS) + (1 if self.vocab_parallel else 0)
         for L in self.layers:
             n += 3
             for name in ("qkv", "o", "gu", "down"):
