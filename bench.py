@@ -835,7 +835,7 @@ def main() -> None:
                          "loaded when present, else generated and saved there")
     ap.add_argument("--layout", choices=["auto", "cm", "kmajor"], default="auto",
                     help="int4 weight layout of the decode projections: tiled column-major (tcgen05 kernel), "
-                         "the reference's K-major (mma.sync kernel), or auto (column-major for batches 9..64)")
+                         "the reference's K-major (mma.sync kernel), or auto (column-major for batches 9..128)")
     ap.add_argument("--profile-case", default=None,
                     choices=["gemv", "gemv_cm", "gemm", "attention", "rmsnorm", "swiglu"],
                     help="instead of the benchmark: one kernel on a bounded case (--m/--k/--n), for an ncu capture")

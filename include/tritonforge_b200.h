@@ -265,7 +265,8 @@ size_t tf_int4_cm_bytes(int64_t N, int64_t K_pad);
 int tf_repack_int4_cm(const uint8_t* packed, uint8_t* packed_cm, int64_t N, int64_t K_pad, void* stream);
 
 /* tf_qlinear_cm: tf_qlinear on tiled column-major weights (tf_repack_int4_cm),
- * decode regime: 1 <= M <= 64, x and scales/zeros of the same 16-bit type,
+ * decode regime: any M >= 1 (one launch per 64 rows, each streaming the
+ * weights once), x and scales/zeros of the same 16-bit type,
  * K % 64 == 0, group_size % 128 == 0, N % 16 == 0, 16-byte aligned operands.
  * Same outputs as tf_qlinear within the floating-point contract (weights
  * dequantised bit-exactly, fp32 accumulation, the same roundings); computed

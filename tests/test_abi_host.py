@@ -184,10 +184,11 @@ def test_colmajor_entry_points_validate_without_a_gpu():
     assert lib.tf_repack_int4_cm(None, None, 64, 128, None) == _lib.ERR_BAD_ARG  # null pointers
     assert lib.tf_repack_int4_cm(None, None, 0, 128, None) == 0  # empty: no-op
     assert lib.tf_qlinear_cm_workspace_bytes(32, 8192, 8192) >= 256
-    # M = 65 is outside the kernel's range: rejected as unsupported before launching
+    # rows not 16-byte aligned (ldx % 8 != 0) are outside the kernel's range:
+    # rejected as unsupported before launching (any M runs, 64 rows per launch)
     x = ctypes.c_void_p(16)
-    rc = lib.tf_qlinear_cm(x, 256, 1, x, x, x, 1, None, 0, x, 128, 65, 128, 256, 256, 128, x, 256, None)
-    assert rc == _lib.ERR_UNSUPPORTED and b"M <= 64" in lib.tf_last_error_message()
+    rc = lib.tf_qlinear_cm(x, 257, 1, x, x, x, 1, None, 0, x, 128, 65, 128, 256, 256, 128, x, 256, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"aligned rows" in lib.tf_last_error_message()
     rc = lib.tf_qlinear_cm_swiglu(x, 256, 1, x, x, x, 1, x, 64, 4, 192, 256, 256, 128, x, 256, None)
     assert rc == _lib.ERR_BAD_SHAPE  # N % 128
 

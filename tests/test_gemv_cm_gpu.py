@@ -37,7 +37,8 @@ def _inputs(m, n, k, dtype, group=128, bias=True, seed=0, w_std=0.02):
 
 CM_SHAPES = [(1, 128, 128), (1, 896, 896), (3, 4864, 896), (16, 1152, 3584), (17, 256, 1024), (5, 1024, 1216),
              (2, 64, 256), (32, 8192, 8192), (9, 8192, 29568), (32, 1280, 8192), (33, 1024, 2048), (64, 896, 896),
-             (48, 3584, 18944), (4, 32768, 384), (2, 4096, 128)]
+             (48, 3584, 18944), (4, 32768, 384), (2, 4096, 128), (100, 3584, 3584), (128, 1024, 2048),
+             (65, 512, 8192)]
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -72,7 +73,7 @@ def test_qlinear_cm_group256_strided_x_out(dtype):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("m,i,k", [(1, 4864, 896), (8, 4864, 896), (3, 896, 4864), (16, 18944, 3584),
                                    (32, 7424, 8192), (5, 1024, 29568), (4, 960, 1024), (64, 1024, 2048),
-                                   (6, 16384, 384)])
+                                   (6, 16384, 384), (100, 1024, 2048)])
 def test_qlinear_cm_swiglu(m, i, k, dtype):
     g = torch.Generator().manual_seed(m + i)
     x = torch.randn(m, k, generator=g).to(dtype).cuda()
@@ -93,13 +94,15 @@ def test_qlinear_cm_swiglu(m, i, k, dtype):
 def test_qlinear_cm_rejects_unsupported():
     x, packed, scales, zeros, _ = _inputs(65, 128, 256, torch.bfloat16, bias=False)
     pcm = colmajor.repack_cm(packed)
+    odd = torch.zeros(65, 257, dtype=torch.bfloat16, device="cuda")[:, :256]  # rows not 16-byte aligned
+    odd.copy_(x)
     with pytest.raises(RuntimeError, match="qlinear_cm"):
-        colmajor.quantized_linear_cm(x, pcm, scales, zeros)
+        colmajor.quantized_linear_cm(odd, pcm, scales, zeros)
     with pytest.raises(ValueError):
         colmajor.quantized_linear_cm(x[:4].half(), pcm, scales, zeros)
 
 
-@pytest.mark.parametrize("batch", [16, 48])
+@pytest.mark.parametrize("batch", [16, 48, 100])
 def test_decoder_colmajor_matches_kmajor(batch):
     """The decode engine on tiled column-major weights (tcgen05 kernel) against
     the same engine on the reference's K-major packing (mma.sync / GEMM
@@ -113,10 +116,11 @@ def test_decoder_colmajor_matches_kmajor(batch):
 
     w = QwenWeights.synthetic("7b", dtype=torch.bfloat16, device=torch.device("cuda", 0), seed=5, layers=2)
     a = QwenDecoder(w, batch, 96, colmajor=False)
-    b = QwenDecoder(w, batch, 96)  # batch 9..64: column-major by default
+    b = QwenDecoder(w, batch, 96)  # batch 9..128: column-major by default
     assert isinstance(a.layers[0]["qkv"], QuantLinear) and isinstance(w.layers[0]["gu"], QuantLinear)
     assert all(isinstance(b.layers[0][n], CMLinear) for n in ("qkv", "o", "gu", "down"))
-    assert b.launches_per_step() == 7 * 2 + 3  # + embedding gather, first norm, lm_head + argmax
+    per = -(-batch // 64)  # launches per projection and per lm_head + argmax: one per 64 rows
+    assert b.launches_per_step() == (3 + 4 * per) * 2 + 2 + per  # + embedding gather, first norm
     for d in (a, b):
         d.fill_cache(40, seed=2)
     for _ in range(3):

@@ -62,7 +62,7 @@ def test_prefill_needs_k_major_projections():
     from tritonforge_b200.decode import QwenDecoder, QwenWeights
 
     w = QwenWeights.synthetic("7b", dtype=torch.bfloat16, device=torch.device("cuda", 0), seed=3, layers=1)
-    d = QwenDecoder(w, 16, 64)  # batches 9..64: column-major projections
+    d = QwenDecoder(w, 16, 64)  # batches 9..128: column-major projections
     with pytest.raises(RuntimeError, match="K-major"):
         d.prefill_tokens(torch.zeros(16, 8, dtype=torch.long))
 

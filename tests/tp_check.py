@@ -139,7 +139,7 @@ def _nccl_main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    B, T = int(os.environ.get("TP_CHECK_BATCH", "4")), 96  # 9..64: the column-major tcgen05 decode kernel
+    B, T = int(os.environ.get("TP_CHECK_BATCH", "4")), 96  # 9..128: the column-major tcgen05 decode kernel
     full = QwenWeights.synthetic(name, tp=1, rank=0, dtype=torch.bfloat16, device=dev, seed=3, layers=layers)
     ref = QwenDecoder(full, B, T)
     ref.fill_cache(40, seed=5)  # same seed on every rank -> same cache everywhere

@@ -64,7 +64,8 @@ def _check(x, packed_cm, scales, zeros):
 def quantized_linear_cm(x: torch.Tensor, packed_cm: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                         bias: torch.Tensor | None = None, group_size: int = 128, *,
                         out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [M, K] @ W (+ bias) with W given column-major (``repack_cm``); M <= 64."""
+    """x [M, K] @ W (+ bias) with W given column-major (``repack_cm``); one
+    kernel launch per 64 rows."""
     dev = _lib.require_cuda(x, packed_cm, scales, zeros, bias)
     _check(x, packed_cm, scales, zeros)
     m, k = x.shape
@@ -82,7 +83,8 @@ def quantized_linear_cm(x: torch.Tensor, packed_cm: torch.Tensor, scales: torch.
 
 def qlinear_cm_swiglu(x: torch.Tensor, packed_cm: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                       group_size: int = 128, *, out: torch.Tensor | None = None) -> torch.Tensor:
-    """silu(x @ Wg) * (x @ Wu) for gate/up interleaved per 64 columns, column-major; M <= 64."""
+    """silu(x @ Wg) * (x @ Wu) for gate/up interleaved per 64 columns,
+    column-major; one kernel launch per 64 rows."""
     dev = _lib.require_cuda(x, packed_cm, scales, zeros)
     _check(x, packed_cm, scales, zeros)
     m, k = x.shape

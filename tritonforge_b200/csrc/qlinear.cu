@@ -147,6 +147,31 @@ extern "C" int tf_qlinear_swiglu(const void* x, int64_t ldx, int x_dtype, const 
   return fail(TF_ERR_UNSUPPORTED, "qlinear_swiglu: no regime takes this problem (alignment or dtypes)");
 }
 
+namespace tf {
+namespace {
+
+// The column-major kernel takes up to 64 rows; more rows run as 64-row chunks
+// (one launch each, each streaming the weights once).
+constexpr int64_t kCmChunkRows = 64;
+
+int gemv_cm_rows_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu, const char* what) {
+  const int64_t osz = pb.out_f32 ? 4 : 2;
+  for (int64_t r = 0; r < pb.M; r += kCmChunkRows) {
+    QLinearProblem c = pb;
+    c.M = pb.M - r < kCmChunkRows ? pb.M - r : kCmChunkRows;
+    c.x = static_cast<const uint8_t*>(pb.x) + r * pb.ldx * 2;
+    c.out = static_cast<uint8_t*>(pb.out) + r * pb.ldo * osz;
+    if (!gemv_cm_supported(c))
+      return fail(TF_ERR_UNSUPPORTED, "%s: needs x and scales of one 16-bit type, K %% 64 == 0, aligned rows", what);
+    const int rc = gemv_cm_launch(c, st, swiglu);
+    if (rc != TF_OK) return rc;
+  }
+  return TF_OK;
+}
+
+}  // namespace
+}  // namespace tf
+
 extern "C" size_t tf_qlinear_cm_workspace_bytes(int64_t M, int64_t N, int64_t K_pad) {
   return tf::gemv_cm_workspace_bytes(M, N, K_pad);
 }
@@ -161,9 +186,7 @@ extern "C" int tf_qlinear_cm(const void* x, int64_t ldx, int x_dtype, const uint
                     K_pad, group_size, workspace, workspace_bytes};
   int rc = validate(pb);
   if (rc != TF_OK || M == 0 || N == 0) return rc;
-  if (!gemv_cm_supported(pb))
-    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
-  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream));
+  return gemv_cm_rows_launch(pb, static_cast<cudaStream_t>(stream), false, "qlinear_cm");
 }
 
 extern "C" int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed_cm,
@@ -180,9 +203,7 @@ extern "C" int tf_qlinear_cm_swiglu(const void* x, int64_t ldx, int x_dtype, con
   if (M == 0 || N == 0) return TF_OK;
   pb.ldo = ldo;
   if (N % 128 != 0) return fail(TF_ERR_BAD_SHAPE, "qlinear_cm_swiglu: N=%lld not a multiple of 128", (long long)N);
-  if (!gemv_cm_supported(pb))
-    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm_swiglu: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
-  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream), true);
+  return gemv_cm_rows_launch(pb, static_cast<cudaStream_t>(stream), true, "qlinear_cm_swiglu");
 }
 
 extern "C" int tf_qlinear_partial(const void* x, int64_t ldx, int x_dtype, const uint8_t* packed, const void* scales,
@@ -206,7 +227,5 @@ extern "C" int tf_qlinear_cm_partial(const void* x, int64_t ldx, int x_dtype, co
                     M,    N,       K,       K_pad,     group_size, workspace, workspace_bytes, 1};
   int rc = validate(pb);
   if (rc != TF_OK || M == 0 || N == 0) return rc;
-  if (!gemv_cm_supported(pb))
-    return fail(TF_ERR_UNSUPPORTED, "qlinear_cm_partial: needs M <= 64, x and scales of one 16-bit type, K %% 64 == 0");
-  return gemv_cm_launch(pb, static_cast<cudaStream_t>(stream));
+  return gemv_cm_rows_launch(pb, static_cast<cudaStream_t>(stream), false, "qlinear_cm_partial");
 }

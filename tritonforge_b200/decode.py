@@ -304,8 +304,10 @@ class QwenDecoder:
     `group` is a torch.distributed process group, or any object with an
     `all_reduce(tensor)` method that sums in place across the ranks."""
 
-    # batches the tcgen05 decode kernel (tiled column-major weights) serves
-    COLMAJOR_BATCH = (9, 64)
+    # batches the tcgen05 decode kernel (tiled column-major weights) serves:
+    # one launch per 64 rows; at 65..128 rows its two launches still beat four
+    # 32-row chunks of the K-major kernel
+    COLMAJOR_BATCH = (9, 128)
 
     def __init__(self, model_or_weights, batch: int, max_len: int, group=None, vocab_parallel: bool | None = None,
                  fused_allreduce: bool | None = None, colmajor: bool | None = None):
@@ -366,7 +368,6 @@ class QwenDecoder:
             "q": torch.empty(B, self.Hq, self.D, dtype=dt, device=dev),
             "attn": torch.empty(B, self.Hq * self.D, dtype=dt, device=dev),
             "o": torch.empty(B, self.H, dtype=dt, device=dev),
-            "gu": torch.empty(B, 2 * self.I, dtype=dt, device=dev),
             "act": torch.empty(B, self.I, dtype=dt, device=dev),
             "mlp": torch.empty(B, self.H, dtype=dt, device=dev),
             "logits": torch.empty(B, self.lm_head.shape[0], dtype=dt, device=dev),
@@ -617,9 +618,9 @@ class QwenDecoder:
         """act = silu(x @ Wg) * (x @ Wu) in one int4 linear with the SwiGLU
         fused: tf_qlinear_swiglu on K-major weights (any rows: decode GEMV,
         its 32-row chunks, or the GEMM with a SwiGLU epilogue),
-        tf_qlinear_cm_swiglu on column-major weights (up to 64 rows)."""
+        tf_qlinear_cm_swiglu on column-major weights (64 rows per launch)."""
         m, k = x.shape
-        if isinstance(ql, CMLinear) and m <= 64:
+        if isinstance(ql, CMLinear):
             qlinear_cm_swiglu(x, ql.tiles, ql.scales, ql.zeros, ql.group_size, out=act)
             return
         if isinstance(ql, QuantLinear):
@@ -630,22 +631,23 @@ class QwenDecoder:
                 _lib.dtype_code(ql.scales.dtype), act.data_ptr(), act.stride(0), m, n, k, kp, ql.group_size,
                 ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.dev)), "qlinear_swiglu")
             return
-        gu = self._lin(x, ql, self.buf["gu"]).view(m, -1, 2, 64)
-        kernels.swiglu(gu[:, :, 0], gu[:, :, 1], out=act.view(m, -1, 64))
+        raise TypeError(f"gate|up projection of unknown type {type(ql).__name__}")
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one step: the embedding gather,
         the first RMSNorm, per layer the four projections (gate|up with its
-        SwiGLU fused; K-major projections of 33..128 rows run as 32-row chunks,
-        one launch each), attention and the two residual + norm (or fused
+        SwiGLU fused; column-major projections launch once per 64 rows,
+        K-major ones of 33..128 rows once per 32-row chunk), attention and the two residual + norm (or fused
         all-reduce) launches, then the lm_head + argmax and, under
         vocabulary-parallel tensor parallelism, best_of_ranks."""
         n = 2 + -(-self.B // self.HEAD_ROWS) + (1 if self.vocab_parallel else 0)
         for L in self.layers:
             n += 3
             for name in ("qkv", "o", "gu", "down"):
-                chunked = not isinstance(L[name], CMLinear) and 32 < self.B <= 128
-                n += -(-self.B // 32) if chunked else 1
+                if isinstance(L[name], CMLinear):
+                    n += -(-self.B // 64)
+                else:
+                    n += -(-self.B // 32) if 32 < self.B <= 128 else 1
         return n
 
     @torch.no_grad()
