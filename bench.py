@@ -756,6 +756,8 @@ def profile_case(args) -> None:
                       context k positions, bf16
       rmsnorm         rmsnorm_residual over [m, n], bf16
       swiglu          swiglu over [m, n], bf16
+      prefill         QwenDecoder.prefill_tokens of an m-token prompt through k
+                      Qwen2.5-7B-shaped layers (synthetic int4 weights), bf16
     """
     import torch
 
@@ -802,6 +804,16 @@ def profile_case(args) -> None:
         out = torch.empty_like(a)
         for _ in range(3):
             kernels.swiglu(a, b_, out=out)
+    elif case == "prefill":
+        from tritonforge_b200.decode import QwenDecoder, QwenWeights
+
+        w = QwenWeights.synthetic("7b", dtype=dt, device=dev, seed=0, layers=k)
+        dec = QwenDecoder(w, 1, m + 8, colmajor=False)
+        prompt = torch.randint(0, w.embed.shape[0], (1, m), generator=torch.Generator().manual_seed(0))
+        for _ in range(3):
+            dec.prefill_tokens(prompt)
+        if dec.device_errors():
+            raise SystemExit("a bounded device wait gave up")
     else:
         raise SystemExit(f"unknown profile case {case!r}")
     torch.cuda.synchronize(dev)
@@ -837,7 +849,7 @@ def main() -> None:
                     help="int4 weight layout of the decode projections: tiled column-major (tcgen05 kernel), "
                          "the reference's K-major (mma.sync kernel), or auto (column-major for batches 9..128)")
     ap.add_argument("--profile-case", default=None,
-                    choices=["gemv", "gemv_cm", "gemm", "attention", "rmsnorm", "swiglu"],
+                    choices=["gemv", "gemv_cm", "gemm", "attention", "rmsnorm", "swiglu", "prefill"],
                     help="instead of the benchmark: one kernel on a bounded case (--m/--k/--n), for an ncu capture")
     ap.add_argument("--m", type=int, default=32)
     ap.add_argument("--k", type=int, default=8192)
