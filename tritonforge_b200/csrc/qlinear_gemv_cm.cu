@@ -1,6 +1,7 @@
 // Decode-regime int4 linear on the 5th-generation tensor cores:
-// out[M, N] = x[M, K] @ W[K, N] (+ bias), M <= 64, for weights repacked into
-// tiles (`tf_repack_int4_cm`).
+// out[M, N] = x[M, K] @ W[K, N] (+ bias), M <= 64 per launch (the entry
+// points launch once per 64 rows), for weights repacked into tiles
+// (`tf_repack_int4_cm`).
 //
 // The reference's decode path is the same Triton kernel as its prefill path
 // (src/tritonforge/kernels/dequant_gemm.py:39-113); its format stores the

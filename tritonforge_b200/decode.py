@@ -727,7 +727,7 @@ class QwenDecoder:
         projection with SwiGLU in its epilogue (tf_qlinear_swiglu), and the lm_head +
         argmax of the last positions. Sets the first generated tokens and the
         position; needs the reference's K-major projections (QuantLinear; the
-        column-major layout serves up to 64 rows)."""
+        column-major kernel is a decode kernel, 64 rows per launch)."""
         import torch.nn.functional as F
 
         if prompt.shape[0] != self.B:
