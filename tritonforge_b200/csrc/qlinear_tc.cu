@@ -30,6 +30,8 @@
 // Every mbarrier wait is bounded (1 s): on expiry the kernel records an error
 // bit in the workspace header, stops issuing work, waits (bounded) for what is
 // in flight, frees its TMEM and finishes.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "qlinear.cuh"
 #include "tcgen05.cuh"
@@ -567,6 +569,302 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// The CTA-pair build: two CTAs of a 2-CTA cluster share one 256-column tile
+// of 512 rows. The even CTA issues tcgen05.mma.cta_group::2 (M = 256: 128 rows
+// in each CTA's tensor memory, N = 256 with each CTA holding 128 columns of
+// B), so each CTA dequantises half of the tile's weights and its shared
+// memory serves half of B. Per 64-k chunk and CTA: x tiles [2 x 128 rows x 64
+// k] and the packed [32 rows x 128 columns] half by TMA (signalled on the
+// CTA's own barrier), 8 dequantisation warps write the [64 k x 128 n] half
+// and arrive on the CTA's own barrier; in the odd CTA one thread forwards
+// that to the even CTA's barrier, whose MMA thread then issues both row
+// tiles' MMAs and commits the slot's release and the accumulators'
+// completion to the barriers of both CTAs. Each CTA reads its own
+// accumulator rows back in the epilogue.
+// ---------------------------------------------------------------------------
+constexpr int kPN = kN / 2;                      // weight columns per CTA of a pair
+constexpr int kPStages = 4;
+constexpr int kPBOff = kMaxTiles * kXTile;       // after the x tiles
+constexpr int kPBBytes = kKC * kPN * 2;          // [64 k][128 n]: 2 atoms of 64 n
+constexpr int kPWOff = kPBOff + kPBBytes;
+constexpr int kPWBytes = (kKC / 2) * kPN;        // packed [32 rows][128 B]
+constexpr int kPSOff = kPWOff + kPWBytes;
+constexpr int kPZOff = kPSOff + kPN * 2;
+constexpr int kPStage = ((kPZOff + kPN * 2) + 1023) / 1024 * 1024;
+static_assert(kPStages * kPStage >= kDeqWarps * kEpiStage, "the epilogue stages in the ring");
+static_assert(kDeqWarps * 32 * 2 == (kKC / 2) * (kPN / 8),
+              "pair dequantisation: 2 items (one packed row x 8 columns) per thread");
+
+template <typename XT, bool kSwiGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_int4_tc_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                             const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap,
+                             const __grid_constant__ CUtensorMap omap, const Args args) {
+  using D = Deq<XT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPStages * kPStage);  // this CTA's copies landed
+  uint64_t* bready = full + kPStages;   // this CTA's half dequantised (even CTA: + the odd CTA's, forwarded)
+  uint64_t* freed = bready + kPStages;  // the slot's pair MMAs completed (committed to both CTAs)
+  uint64_t* accum = freed + kPStages;   // every pair MMA completed (committed to both CTAs)
+  uint64_t* alldone = accum + 1;        // every warp of this CTA finished its role
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(alldone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();         // 0: the pair's MMA issuer
+  const int n0 = (int)(blockIdx.x >> 1) * kN;       // the pair's output columns
+  const int nw = n0 + (int)rank * kPN;              // this CTA's weight columns
+  const int m0 = blockIdx.y * (2 * kMT * kMaxTiles);  // the pair's 512 rows
+  int ptiles = (args.M - m0 + 2 * kMT - 1) / (2 * kMT);  // pair row tiles of 256 rows
+  if (ptiles > kMaxTiles) ptiles = kMaxTiles;
+  const int nc = args.n_chunks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&bready[i], 2 * kDeqWarps);
+      mbar_init(&freed[i], 1);
+    }
+    mbar_init(accum, 1);
+    mbar_init(alldone, kThreads / 32);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0) {
+    // the same 512 columns in both CTAs: 2 row tiles x 256 fp32 accumulator columns
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == kDeqWarps) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      prefetch_tensormap(&xmap);
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&smap);
+      prefetch_tensormap(&zmap);
+      pdl_wait();
+      const uint32_t tx = (uint32_t)(ptiles * kXTile + kPWBytes + 2 * kPN * 2);
+      int issued = 0;
+      for (int c = 0; c < nc; ++c) {
+        const int slot = c % kPStages;
+        if (c >= kPStages &&
+            !mbar_wait_bounded(&freed[slot], (uint32_t)(c / kPStages - 1) & 1u, args.err, 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        uint8_t* st = smem + slot * kPStage;
+        mbar_arrive_expect_tx(&full[slot], tx);
+        for (int t = 0; t < ptiles; ++t)
+          tma_load_2d(st + t * kXTile, &xmap, &full[slot], c * kKC, m0 + t * 2 * kMT + (int)rank * kMT);
+        tma_load_2d(st + kPWOff, &wmap, &full[slot], nw, c * (kKC / 2));
+        const int grow = (c * kKC) / args.group_size;
+        tma_load_2d(st + kPSOff, &smap, &full[slot], nw, grow);
+        tma_load_2d(st + kPZOff, &zmap, &full[slot], nw, grow);
+        issued = c + 1;
+      }
+      if (*abort_flag) {
+        for (int c = (issued > kPStages ? issued - kPStages : 0); c < issued; ++c)
+          mbar_wait_bounded(&full[c % kPStages], (uint32_t)(c / kPStages) & 1u, args.err, 4);
+      }
+    }
+  } else if (warp == kDeqWarps + 1) {
+    // ------------------------------------------------- MMA (even CTA only)
+    if (lane == 0 && rank == 0) {
+      for (int c = 0; c < nc; ++c) {
+        const int slot = c % kPStages;
+        const uint32_t ph = (uint32_t)(c / kPStages) & 1u;
+        if (*abort_flag) break;
+        if (!mbar_wait_bounded(&full[slot], ph, args.err, 2) ||
+            !mbar_wait_bounded(&bready[slot], ph, args.err, 2)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + slot * kPStage);
+#pragma unroll
+        for (int ks = 0; ks < kKC / 16; ++ks) {
+          // B: this CTA's [64 k x 128 n] half, MN-major 64-n atoms (LBO 8 KiB, SBO 1 KiB);
+          // the peer's half sits at the same offset
+          const uint64_t bdesc = umma_desc(st + kPBOff + ks * 2048, 8192, 1024);
+          for (int t = 0; t < ptiles; ++t) {
+            const uint64_t adesc = umma_desc(st + t * kXTile + ks * 32, 16, 1024);
+            umma_f16_pair(tmem + t * kN, adesc, bdesc, args.idesc, (c > 0 || ks > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit_pair(&freed[slot]);
+      }
+      umma_commit_pair(accum);
+      mbar_wait_bounded(accum, 0u, args.err, 8);  // this warp reports done only after them
+    }
+  } else {
+    // ------------------------------------------------------ dequantisation
+    const int tid = threadIdx.x;                 // 0..255
+    const int cg = tid & 15;                     // columns 8 cg .. 8 cg + 7 of this CTA's half
+    for (int c = 0; c < nc; ++c) {
+      const int slot = c % kPStages;
+      if (*abort_flag) break;
+      if (!mbar_wait_bounded(&full[slot], (uint32_t)(c / kPStages) & 1u, args.err, 2)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* st = smem + slot * kPStage;
+      const uint4 s4 = *reinterpret_cast<const uint4*>(st + kPSOff + 16 * cg);
+      const uint4 z4 = *reinterpret_cast<const uint4*>(st + kPZOff + 16 * cg);
+      const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, zw[4] = {z4.x, z4.y, z4.z, z4.w};
+      uint32_t zlo[4], zhi[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        zlo[p] = D::add(zw[p], D::off_lo());
+        zhi[p] = D::add(zw[p], D::off_hi());
+      }
+#pragma unroll
+      for (int item = 0; item < 2; ++item) {
+        const int j = (tid >> 4) + 16 * item;  // packed row: k = 2j, 2j + 1 of the chunk
+        const uint2 pw = *reinterpret_cast<const uint2*>(st + kPWOff + j * kPN + 8 * cg);
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t word = p < 2 ? pw.x : pw.y;
+          const uint32_t tt = __byte_perm(word, 0u, (p & 1) ? 0x4342u : 0x4140u);
+          lo[p] = D::mul(D::sub(D::lo(tt), zlo[p]), sw[p]);  // k = 2j
+          hi[p] = D::mul(D::sub(D::hi(tt), zhi[p]), sw[p]);  // k = 2j + 1
+        }
+        // MN-major swizzled half tile: atom cg / 8 (64 columns), row k, 16-byte chunk (cg % 8) ^ (k % 8)
+        uint8_t* b = st + kPBOff + (cg >> 3) * 8192;
+        const int k0 = 2 * j, k1 = 2 * j + 1;
+        *reinterpret_cast<uint4*>(b + k0 * 128 + (((cg & 7) ^ (k0 & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(b + k1 * 128 + (((cg & 7) ^ (k1 & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      // make the generic-proxy stores visible to the tensor core, then signal
+      // the even CTA (the odd CTA's warps remotely)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&bready[slot]);
+        else mbar_arrive_cluster(mapa_shared(&bready[slot], 0));
+      }
+    }
+
+    // ------------------------------------------------------------ epilogue
+    // As the one-tile-per-CTA build: warp w reads TMEM lanes 32 (w % 4) .. of
+    // each row tile (this CTA's 128 rows of the pair tile) and 128 columns,
+    // stages them in its 16 KiB of the idle ring and stores them with TMA.
+    if (mbar_wait_bounded(accum, 0u, args.err, 8)) {
+      tc_fence_after();
+      pdl_wait();  // output writes follow the previous kernel
+      const int quad = warp & 3, c_base = (warp >> 2) * (kN / 2);
+      const uint32_t rsw = (uint32_t)(lane & 7);
+      uint8_t* stage = smem + warp * kEpiStage;
+      const int box_cols = args.out_f32 ? 32 : 64;
+      for (int t = 0; t < ptiles; ++t) {
+        if (t > 0) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
+        const uint32_t tbase = tmem + ((uint32_t)(32 * quad) << 16) + t * kN;
+        if constexpr (kSwiGLU) {
+          for (int lc = 0; lc < 64; lc += 32) {
+            uint32_t gr[32], ur[32], h[16];
+            tmem_ld32(tbase + c_base + lc, gr);
+            tmem_ld32(tbase + c_base + 64 + lc, ur);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float o[2];
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const float gv = round_to<XT>(__uint_as_float(gr[e + i]));
+                const float uv = round_to<XT>(__uint_as_float(ur[e + i]));
+                const float sig = 1.0f / (1.0f + expf(-gv));
+                o[i] = (gv * sig) * uv;
+              }
+              const XT a = Num<XT>::from_f(o[0]), b = Num<XT>::from_f(o[1]);
+              h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
+                         ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
+            }
+            uint8_t* srow = stage + lane * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(srow + (((uint32_t)(lc / 8 + q) ^ rsw) << 4)) =
+                  make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+          }
+        } else {
+          for (int lc = 0; lc < kN / 2; lc += 32) {
+            const int cc = c_base + lc;
+            uint32_t r[32];
+            tmem_ld32(tbase + cc, r);
+            if (args.out_f32) {
+              uint8_t* srow = stage + (lc / 32) * 4096 + lane * 128;
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<uint4*>(srow + (((uint32_t)q ^ rsw) << 4)) =
+                    make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            } else {
+              uint32_t h[16];
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float v0 = round_to<XT>(__uint_as_float(r[e])), v1 = round_to<XT>(__uint_as_float(r[e + 1]));
+                if (args.bias) {
+                  const int col = n0 + cc + e;
+                  if (col < args.N) v0 += load_as_f32(args.bias, col, args.bias_dtype);
+                  if (col + 1 < args.N) v1 += load_as_f32(args.bias, col + 1, args.bias_dtype);
+                }
+                const XT a = Num<XT>::from_f(v0), b = Num<XT>::from_f(v1);
+                h[e / 2] = (uint32_t)reinterpret_cast<const uint16_t&>(a) |
+                           ((uint32_t)reinterpret_cast<const uint16_t&>(b) << 16);
+              }
+              uint8_t* srow = stage + (lc / 64) * 4096 + lane * 128;
+              const int c0 = (lc % 64) / 8;
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(srow + (((uint32_t)(c0 + q) ^ rsw) << 4)) =
+                    make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+            }
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          const int row0 = m0 + t * 2 * kMT + (int)rank * kMT + 32 * quad;
+          if constexpr (kSwiGLU) {
+            tma_store_2d(&omap, stage, (n0 + c_base) / 2, row0);
+          } else {
+            for (int b = 0; b < (kN / 2) / box_cols; ++b)
+              tma_store_2d(&omap, stage + b * 4096, n0 + c_base + b * box_cols, row0);
+          }
+          bulk_commit_group();
+        }
+      }
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+    }
+  }
+  // Teardown: each warp converges and reports on an mbarrier that warp 0 waits
+  // for (bounded); then the whole pair meets at a cluster barrier (the peer's
+  // MMAs read this CTA's shared memory and write its tensor memory until the
+  // accumulators complete) before both CTAs free the tensor memory.
+  __syncwarp();
+  tc_fence_before();
+  if (lane == 0) mbar_arrive(alldone);
+  if (warp == 0) mbar_wait_bounded(alldone, 0u, args.err, 64);
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
 }  // namespace tc
 
 bool gemm_supported(const QLinearProblem& pb) {
@@ -597,6 +895,16 @@ struct SkPlan {
   int64_t n_tiles;
   size_t bytes;
 };
+
+// The CTA-pair build serves problems of more than 256 rows on the one tile
+// per CTA schedule; TRITONFORGE_B200_GEMM_PAIR=0 keeps the single-CTA build.
+bool pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("TRITONFORGE_B200_GEMM_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 constexpr int64_t kEpiChunks = 10;
 constexpr int64_t kPieceReadChunks = 14;
@@ -649,6 +957,22 @@ extern "C" int tf_qlinear_gemm_stream_k_grid(int64_t M, int64_t N, int64_t K) {
 }
 
 namespace tf {
+
+template <typename XT, bool kSwiGLU>
+static int launch_gemm_pair(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
+  using namespace tc;
+  auto kern = gemm_int4_tc_pair_kernel<XT, kSwiGLU>;
+  const size_t smem = (size_t)kPStages * kPStage + 1024 + 128;
+  static bool attr_set[64] = {false};  // per instantiation and device
+  const int dev = current_device() & 63;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("gemm pair set smem attribute");
+    attr_set[dev] = true;
+  }
+  return launch_ex("gemm_int4_tc_pair", kern, grid, dim3(kThreads), smem, st, dim3(2, 1, 1), maps[0], maps[1],
+                   maps[2], maps[3], maps[4], a);
+}
 
 template <typename XT, bool kSK, bool kSwiGLU>
 static int launch_gemm(dim3 grid, const CUtensorMap* maps, const tc::Args& a, cudaStream_t st) {
@@ -725,6 +1049,25 @@ int gemm_launch(const QLinearProblem& pb, cudaStream_t st, bool swiglu) {
     grid = dim3((unsigned)plan.grid, 1);
   }
   const bool bf16 = pb.x_dtype == TF_BF16;
+  if (!a.stream_k && pb.M > 2 * kMT && pair_gemm_enabled()) {
+    // CTA pairs on 512-row tiles: the weight, scale and zero maps take the
+    // 128 columns of one CTA
+    rc = encode_tensor_map_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, pb.packed, (uint64_t)pb.N,
+                              (uint64_t)(pb.K_pad / 2), (uint64_t)pb.N, kPN, kKC / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_tensor_map_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.scales, (uint64_t)pb.N, (uint64_t)groups,
+                              (uint64_t)pb.N * 2, kPN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, pb.zeros, (uint64_t)pb.N, (uint64_t)groups,
+                              (uint64_t)pb.N * 2, kPN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    a.idesc = (a.idesc & ~(0x1Fu << 24)) | ((uint32_t)((2 * kMT) >> 4) << 24);  // M = 256 across the pair
+    const dim3 pgrid((unsigned)(2 * a.tiles_n), (unsigned)cdiv(pb.M, (int64_t)2 * kMT * kMaxTiles));
+    if (swiglu) return bf16 ? launch_gemm_pair<__nv_bfloat16, true>(pgrid, maps, a, st)
+                            : launch_gemm_pair<__half, true>(pgrid, maps, a, st);
+    return bf16 ? launch_gemm_pair<__nv_bfloat16, false>(pgrid, maps, a, st)
+                : launch_gemm_pair<__half, false>(pgrid, maps, a, st);
+  }
   if (a.stream_k) {
     if (swiglu) return bf16 ? launch_gemm<__nv_bfloat16, true, true>(grid, maps, a, st)
                             : launch_gemm<__half, true, true>(grid, maps, a, st);
