@@ -478,39 +478,81 @@ size_t decode_attention_smem(int head_dim) {
 
 namespace tf {
 namespace {
-#ifndef TF_ATTN_MAX_CHUNK
-// Positions per CTA at most. Longer chunks amortise a CTA's fixed work (RoPE
-// prologue, warp merge, cluster combine) over more tiles: at 72B batch 32 and
-// 4096 positions, chunks of <= 512 / 2048 / 4096 ran at 3.5 / 4.6 / 5.2 TB/s.
-#define TF_ATTN_MAX_CHUNK 4096
+#ifndef TF_ATTN_FIXED_POSITIONS
+// A CTA's fixed work (launch, RoPE prologue, warp merge, cluster combine) in
+// positions of streamed context. Fitted to CUDA-event times of this kernel:
+// at one CTA per (row, kv head) chunk, time ~ waves x (chunk + 340..680).
+#define TF_ATTN_FIXED_POSITIONS 512
 #endif
+
+// Clusters of `s` CTAs of this kernel resident at once (2 CTAs per SM at
+// 181 registers; clusters stay inside one GPC, so s that do not divide it
+// leave SMs idle).
+template <typename T, int D, bool kRope>
+int attn_resident_clusters(int s, size_t smem) {
+  static int cache[64][9] = {};
+  int& c = cache[current_device() & 63][s];
+  if (c > 0) return c;
+  auto kern = decode_attn_kernel<T, D, kRope>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, (unsigned)s);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = (unsigned)s;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  if (n <= 0) n = 2 * num_sms() / s;
+  if (n <= 0) n = 1;
+  c = n;
+  return n;
+}
+
+// Splits of the context per (row, kv head): the s in 1..8 (chunks of >= 64
+// positions) with the least waves(s) x (chunk(s) + fixed work), waves counted
+// in resident clusters. A CTA streams its chunk at a latency-bound rate, so a
+// partly filled last wave costs as much as a full one: at 72B batch 32 and
+// 4096 positions one split (256 CTAs, one wave) beats two (512 CTAs, two
+// waves), and at 7B batch 32 two splits (one wave) beat three.
+template <typename T, int D, bool kRope>
+int attn_splits(int64_t rows, int64_t t_max, size_t smem) {
+  int64_t best = -1;
+  int pick = 1;
+  for (int s = 1; s <= 8; ++s) {
+    if (s > 1 && cdiv(t_max, s) < 64) break;
+    const int64_t waves = cdiv(rows, (int64_t)attn_resident_clusters<T, D, kRope>(s, smem));
+    const int64_t cost = waves * (cdiv(t_max, s) + TF_ATTN_FIXED_POSITIONS);
+    if (best < 0 || cost < best) {
+      best = cost;
+      pick = s;
+    }
+  }
+  return pick;
+}
 
 template <typename T, bool kRope>
 int launch_attention(const void* q, const void* k_cache, const void* v_cache, void* out, const int* len, int64_t B,
                      int hq, int hkv, int head_dim, int64_t t_max, float scale, const RopeIn<T>& rope,
                      cudaStream_t st) {
-  const int g = hq / hkv;
-  (void)g;
-  // split the context over a cluster: >= 2 CTAs per SM when the batch is
-  // small, and chunks of at most TF_ATTN_MAX_CHUNK positions (up to 8 splits)
   const int64_t rows = B * hkv;
-  int splits = (int)cdiv(2LL * num_sms(), rows);
-  const int by_chunk = (int)cdiv(t_max, TF_ATTN_MAX_CHUNK);
-  if (splits < by_chunk) splits = by_chunk;
-  const int max_by_len = (int)cdiv(t_max, 64);
-  if (splits > max_by_len) splits = max_by_len;
-  if (splits > 8) splits = 8;
-  if (splits < 1) splits = 1;
-  const int chunk = (int)cdiv(t_max, splits);
   const size_t smem = decode_attention_smem(head_dim);
-  const dim3 grid((unsigned)hkv, (unsigned)B, (unsigned)splits), cluster(1, 1, (unsigned)splits);
-  auto go = [&](auto kern) -> int {
+  auto go = [&](auto kern, int splits) -> int {
+    const int chunk = (int)cdiv(t_max, splits);
+    const dim3 grid((unsigned)hkv, (unsigned)B, (unsigned)splits), cluster(1, 1, (unsigned)splits);
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     return launch_ex("decode_attention", kern, grid, dim3(128), smem, st, cluster, (const T*)q, (const T*)k_cache,
                      (const T*)v_cache, (T*)out, len, hq, hkv, (int)t_max, chunk, scale, rope);
   };
-  if (head_dim == 64) return go(decode_attn_kernel<T, 64, kRope>);
-  return go(decode_attn_kernel<T, 128, kRope>);
+  if (head_dim == 64) return go(decode_attn_kernel<T, 64, kRope>, attn_splits<T, 64, kRope>(rows, t_max, smem));
+  return go(decode_attn_kernel<T, 128, kRope>, attn_splits<T, 128, kRope>(rows, t_max, smem));
 }
 
 int check_attention(const void* q, const void* k_cache, const void* v_cache, void* out, const int* len, int64_t B,
